@@ -1,0 +1,320 @@
+"""Benchmark of the fused Waller attention on B200 (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gae|reference]
+                    [--workload mha|mha-noncausal|long]
+
+Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
+  mha            BASELINE config 2, causal: B=4, H=16, N=8192, head_dim=128 (default)
+  mha-noncausal  the same, non-causal
+  long           config 5, causal: one sequence, H=8, head_dim=128, N=131072
+One step = one fused attention forward over the whole batch.  FLOPs count only
+visible (unmasked) score entries: 4*d per (query, key) pair, causal pairs
+N(N+1)/2 per head.  Inputs (3 x 128 MiB for mha) exceed the 126 MB L2, so no
+flush between steps is needed.
+
+--gpus N > 1 (torchrun, one process per GPU): every rank runs its own batch of
+the workload (weak scaling; attention over independent (batch, head) units
+needs no exchange).  Timing: CUDA events on the launching stream, barrier +
+synchronize on both sides, max over ranks.
+
+--impl reference: the reference's CPU attention path (the oracle's restatement
+of rust_src/src/waller_operator.rs, OpenMP over rows like
+waller_operator_parallel) on the host cores, on a bounded sample of the same
+workload (one (batch, head) slice per step), in the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "mha": dict(B=4, H=16, N=8192, D=128, causal=True, cfg="config2-causal"),
+    "mha-noncausal": dict(B=4, H=16, N=8192, D=128, causal=False, cfg="config2-noncausal"),
+    "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
+}
+METRIC = "fused-attention TFLOPS (bf16 d=128)"
+
+
+def attn_flops(B, H, Nq, Nkv, D, causal):
+    pairs = Nq * (Nq + 1) // 2 if causal else Nq * Nkv
+    return 4.0 * D * B * H * pairs
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}, "fallback"
+
+
+def profile_traffic(kernel_tag):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/*.md."""
+    d = os.path.join(ROOT, "profiles")
+    if not os.path.isdir(d):
+        return None
+    for fn in sorted(os.listdir(d)):
+        if not fn.endswith(".md"):
+            continue
+        txt = open(os.path.join(d, fn)).read()
+        m = re.search(r"traffic_bytes_per_launch\[%s\]:\s*([0-9.eE+]+)" % re.escape(kernel_tag), txt)
+        if m:
+            return float(m.group(1))
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(torch, w, device, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    shape = (w["B"], w["H"], w["N"], w["D"])
+    return [torch.randn(*shape, generator=g).to(torch.bfloat16).to(device) for _ in range(3)]
+
+
+def cpu_sample(w, threads_note=True):
+    """Times the oracle's Waller recurrence on one (batch, head) slice of the
+    workload (all query rows, their full causal key range).  Returns
+    (TFLOPS, seconds, description)."""
+    import numpy as np
+    from oracle import oracle
+    N, D = w["N"], w["D"]
+    rng = np.random.default_rng(1234)
+    q, k, v = (rng.standard_normal((1, 1, N, D)).astype(np.float32) for _ in range(3))
+    rows = None
+    n_rows = N
+    if N > 16384:  # long workload: evenly spaced rows, full key range each
+        n_rows = 2048
+        rows = np.linspace(0, N - 1, n_rows).round().astype(np.int64)
+    oracle.lib()
+    t0 = time.perf_counter()
+    oracle.attention_batched(q, k, v, 1.0 / math.sqrt(D), w["causal"], rows=rows)
+    dt = time.perf_counter() - t0
+    if rows is None:
+        flops = attn_flops(1, 1, N, N, D, w["causal"])
+        desc = f"one (batch, head) slice: {N} query rows x full {'causal ' if w['causal'] else ''}key range"
+    else:
+        pairs = float(np.sum(rows + 1)) if w["causal"] else float(n_rows * N)
+        flops = 4.0 * D * pairs
+        desc = f"{n_rows} evenly spaced query rows of one head, full causal key range each"
+    return flops / dt / 1e12, dt, desc, oracle.num_threads()
+
+
+def run_reference(args, w):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    for _ in range(args.warmup):
+        cpu_sample(w)
+    vals, secs = [], []
+    desc, threads = "", 1
+    for _ in range(args.steps):
+        v, s, desc, threads = cpu_sample(w)
+        vals.append(v)
+        secs.append(s)
+    value = statistics.mean(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * statistics.mean(secs), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": w["cfg"], "B": w["B"], "H": w["H"], "seq_len": w["N"],
+                   "head_dim": w["D"], "causal": w["causal"]},
+        "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
+                         "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="gae", choices=["gae", "reference"])
+    ap.add_argument("--workload", default="mha", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        return run_reference(args, w)
+
+    import torch
+    import torch.distributed as dist
+    import __graft_entry__ as ge
+    gae = ge.load_package()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    B, H, N, D, causal = w["B"], w["H"], w["N"], w["D"], w["causal"]
+    q, k, v = make_inputs(torch, w, dev, 1000 + rank)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream()
+    flops = attn_flops(B, H, N, N, D, causal)
+
+    # ---- device-resident timing (value, roofline) -------------------------
+    for _ in range(args.warmup):
+        gae.attention(q, k, v, causal=causal, out=out)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            gae.attention(q, k, v, causal=causal, out=out)
+        ev1.record(stream)
+        barrier()
+    gae.device_status()
+    t_ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = t_ms / args.steps
+    value = world * flops / (ms_step * 1e-3) / 1e12
+
+    # ---- end to end through the public API with host buffers ---------------
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        gae.attention(dq, dk, dv, causal=causal, out=out)
+        hout.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 10))
+    barrier()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
+    e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
+    bytes_in = 3 * q.numel() * q.element_size()
+    bytes_out = out.numel() * out.element_size()
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        dist.destroy_process_group()
+        return 0
+
+    peaks, peak_kind = measured_peaks()
+    achieved = flops / (ms_step * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_kind": f"{peak_kind} bf16 burst",
+                "traffic": profile_traffic(args.workload)}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v_cpu, s_cpu, desc, threads = cpu_sample(w)
+        cpu = {"value": v_cpu, "unit": "TFLOPS", "cores": threads, "kind": "port",
+               "sample": desc + f" ({s_cpu:.1f} s)"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": w["cfg"], "B": B, "H": H, "seq_len": N, "head_dim": D,
+                   "causal": causal, "global_batch": B * world,
+                   "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (no flush)"},
+        "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,
+                "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "pct_of_tensor_peak": 100.0 * achieved / peak,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,410 @@
+"""gae_b200 -- B200-native fused "Waller" attention (host side).
+
+This package is the host-language mirror of the reference crate `ate`
+(RegularJoe-CEO/Geodesic-Attention-Engine-GAE-, rust_src/src/lib.rs:20-30)
+over the C ABI of libgae.so (include/gae.h).  Functions keep the crate's
+names, argument meaning and failure behaviour (the crate panics on bad input;
+here a GAEError is raised).  All attention compute runs in the library's CUDA
+kernels; there is no CPU fallback: importing works without a GPU, but every
+compute call needs libgae.so and a CUDA device and raises otherwise.
+
+Device-tensor entry points (torch tensors on a CUDA device):
+    attention(q, k, v, causal=..., ...)      -> tcgen05 kernel (bf16/f16) or fp32 kernel
+    lse_merge_(o_acc, lse_acc, o_part, lse_part)
+    quantize_rows_int8(x), attention_int8(...), int8_logits(...)
+Host drop-ins of the crate (numpy / sequences of float, fp32):
+    waller_operator, waller_operator_parallel, standard_attention
+Scalar helpers of the crate (pure host logic, not the hot path):
+    OnlineSoftmax, OnlineSoftmaxVec, WelfordState, gelu, silu, relu,
+    GAEConfig, TransformerConfig
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libgae.so")
+
+GAE_OK = 0
+_STATUS = {0: "GAE_OK", 1: "GAE_ERR_INVALID_ARG", 2: "GAE_ERR_UNSUPPORTED", 3: "GAE_ERR_CUDA",
+           4: "GAE_ERR_OOM", 5: "GAE_ERR_COMM", 6: "GAE_ERR_TIMEOUT"}
+DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+
+
+class GAEError(RuntimeError):
+    """A libgae.so entry point returned a non-OK status."""
+
+    def __init__(self, status: int, detail: str):
+        super().__init__(f"{_STATUS.get(status, status)}: {detail}")
+        self.status = status
+
+
+class AttnArgs(C.Structure):
+    """Mirror of gae_attn_args (include/gae.h)."""
+    _fields_ = [
+        ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
+        ("lse", C.c_void_p),
+        ("batch", C.c_int64), ("heads", C.c_int64), ("seq_q", C.c_int64),
+        ("seq_kv", C.c_int64), ("head_dim", C.c_int64),
+        ("q_stride", C.c_int64 * 3), ("k_stride", C.c_int64 * 3),
+        ("v_stride", C.c_int64 * 3), ("o_stride", C.c_int64 * 3),
+        ("dtype", C.c_int), ("causal", C.c_int), ("scale", C.c_float),
+        ("q_offset", C.c_int64), ("kv_offset", C.c_int64),
+    ]
+
+
+class AttnInt8Args(C.Structure):
+    """Mirror of gae_attn_int8_args (include/gae.h)."""
+    _fields_ = [
+        ("q", C.c_void_p), ("k", C.c_void_p), ("q_scale", C.c_void_p), ("k_scale", C.c_void_p),
+        ("v", C.c_void_p), ("o", C.c_void_p), ("lse", C.c_void_p),
+        ("batch_heads", C.c_int64), ("seq", C.c_int64), ("head_dim", C.c_int64),
+        ("causal", C.c_int), ("scale", C.c_float),
+    ]
+
+
+_lib = None
+
+
+def lib():
+    """Loads libgae.so (built by build.py).  Raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise GAEError(3, f"libgae.so not found at {LIB_PATH}; run build.py")
+    L = C.CDLL(LIB_PATH)
+    vp, i64, sz = C.c_void_p, C.c_int64, C.c_size_t
+    L.gae_status_string.restype = C.c_char_p
+    L.gae_status_string.argtypes = [C.c_int]
+    L.gae_last_error.argtypes = [C.c_char_p, sz]
+    L.gae_version.restype = C.c_char_p
+    L.gae_device_status.argtypes = [C.c_int]
+    host = [vp, vp, vp, sz, sz, C.c_float, C.c_int, vp]
+    L.gae_waller_operator_f32_host.argtypes = host
+    L.gae_waller_operator_parallel_f32_host.argtypes = host
+    L.gae_standard_attention_f32_host.argtypes = host
+    L.gae_attn_fwd.argtypes = [C.POINTER(AttnArgs), vp]
+    L.gae_attn_int8_fwd.argtypes = [C.POINTER(AttnInt8Args), vp]
+    L.gae_int8_logits.argtypes = [vp, vp, i64, i64, i64, i64, vp, vp]
+    L.gae_quantize_rows_int8.argtypes = [vp, C.c_int, i64, i64, vp, vp, vp]
+    L.gae_lse_merge.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, C.c_int, vp]
+    L.gae_layer_workspace_bytes.restype = sz
+    L.gae_layer_workspace_bytes.argtypes = [i64, i64, i64, i64]
+    L.gae_layer_fwd.argtypes = [vp, vp, vp]
+    L.gae_layer_stack_fwd.argtypes = [vp, vp, C.c_int, vp]
+    L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
+    _lib = L
+    return L
+
+
+def _check(status: int):
+    if status != GAE_OK:
+        buf = C.create_string_buffer(512)
+        lib().gae_last_error(buf, 512)
+        raise GAEError(status, buf.value.decode(errors="replace"))
+
+
+def version() -> str:
+    return lib().gae_version().decode()
+
+
+def device_status(reset: bool = True):
+    """Raises GAEError(GAE_ERR_TIMEOUT) if a kernel recorded a bounded-wait failure."""
+    _check(lib().gae_device_status(1 if reset else 0))
+
+
+# ---------------------------------------------------------------- torch glue
+def _torch():
+    import torch
+    return torch
+
+
+def _stream_ptr(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _dtype_code(t):
+    torch = _torch()
+    if t.dtype == torch.bfloat16:
+        return DTYPE_BF16
+    if t.dtype == torch.float16:
+        return DTYPE_F16
+    if t.dtype == torch.float32:
+        return DTYPE_F32
+    raise GAEError(1, f"unsupported dtype {t.dtype}")
+
+
+def _bhsd(t, name):
+    if t.dim() != 4:
+        raise GAEError(1, f"{name} must be [batch, heads, seq, head_dim]")
+    if t.stride(-1) != 1:
+        raise GAEError(1, f"{name} must have a contiguous head_dim")
+    if not t.is_cuda:
+        raise GAEError(1, f"{name} must be a CUDA tensor")
+    return (t.stride(0), t.stride(1), t.stride(2))
+
+
+def attention(q, k, v, *, causal: bool = False, scale: float | None = None, q_offset: int = 0,
+              kv_offset: int = 0, out=None, lse=None, return_lse: bool = False, stream=None):
+    """Fused exact attention on device tensors [B, H, N, D] (strided views allowed).
+
+    bf16/f16 -> tcgen05 tensor-core kernel (head_dim 64/128); fp32 -> fp32
+    CUDA-core kernel.  The Waller operator of rust_src/src/waller_operator.rs:8-59
+    generalised to batches, both masks and ring-block offsets.
+    """
+    torch = _torch()
+    B, H, Nq, D = q.shape
+    Nkv = k.shape[2]
+    if k.shape != (B, H, Nkv, D) or v.shape != (B, H, Nkv, D):
+        raise GAEError(1, "k and v must be [B, H, Nkv, D] matching q")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise GAEError(1, "q, k, v must share a dtype")
+    if out is None:
+        out = torch.empty((B, H, Nq, D), dtype=q.dtype, device=q.device)
+    if return_lse and lse is None:
+        lse = torch.empty((B, H, Nq), dtype=torch.float32, device=q.device)
+    if lse is not None and (not lse.is_contiguous() or lse.dtype != torch.float32):
+        raise GAEError(1, "lse must be a contiguous fp32 tensor [B, H, Nq]")
+    a = AttnArgs()
+    a.q, a.k, a.v, a.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    a.lse = lse.data_ptr() if lse is not None else None
+    a.batch, a.heads, a.seq_q, a.seq_kv, a.head_dim = B, H, Nq, Nkv, D
+    a.q_stride[:] = _bhsd(q, "q")
+    a.k_stride[:] = _bhsd(k, "k")
+    a.v_stride[:] = _bhsd(v, "v")
+    a.o_stride[:] = _bhsd(out, "out")
+    a.dtype = _dtype_code(q)
+    a.causal = 1 if causal else 0
+    a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    a.q_offset, a.kv_offset = int(q_offset), int(kv_offset)
+    _check(lib().gae_attn_fwd(C.byref(a), _stream_ptr(stream)))
+    return (out, lse) if return_lse else out
+
+
+def lse_merge_(o_acc, lse_acc, o_part, lse_part, stream=None):
+    """In-place log-sum-exp merge of a partial result into an accumulator."""
+    D = o_acc.shape[-1]
+    rows = o_acc.numel() // D
+    if o_part.shape != o_acc.shape or lse_acc.numel() != rows or lse_part.numel() != rows:
+        raise GAEError(1, "lse_merge_: shape mismatch")
+    if not (o_acc.is_contiguous() and o_part.is_contiguous()):
+        raise GAEError(1, "lse_merge_: outputs must be contiguous")
+    _check(lib().gae_lse_merge(o_acc.data_ptr(), lse_acc.data_ptr(), o_part.data_ptr(),
+                               lse_part.data_ptr(), rows, D, D, D, _dtype_code(o_acc),
+                               _stream_ptr(stream)))
+    return o_acc, lse_acc
+
+
+def quantize_rows_int8(x, stream=None):
+    """Per-row symmetric int8 quantisation of a contiguous [..., d] bf16/fp32 tensor."""
+    torch = _torch()
+    x = x.contiguous()
+    d = x.shape[-1]
+    rows = x.numel() // d
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    _check(lib().gae_quantize_rows_int8(x.data_ptr(), _dtype_code(x), rows, d, q.data_ptr(),
+                                        s.data_ptr(), _stream_ptr(stream)))
+    return q, s
+
+
+def attention_int8(q, k, q_scale, k_scale, v, *, causal=False, scale=None, out=None,
+                   return_lse=False, stream=None):
+    """INT8 attention: q, k int8 [BH, N, D] + fp32 row scales [BH, N]; v bf16 [BH, N, D]."""
+    torch = _torch()
+    BH, N, D = q.shape
+    if out is None:
+        out = torch.empty((BH, N, D), dtype=torch.bfloat16, device=q.device)
+    lse = torch.empty((BH, N), dtype=torch.float32, device=q.device) if return_lse else None
+    for t in (q, k, q_scale, k_scale, v, out):
+        if not t.is_contiguous():
+            raise GAEError(1, "attention_int8: tensors must be contiguous")
+    a = AttnInt8Args()
+    a.q, a.k, a.q_scale, a.k_scale = q.data_ptr(), k.data_ptr(), q_scale.data_ptr(), k_scale.data_ptr()
+    a.v, a.o = v.data_ptr(), out.data_ptr()
+    a.lse = lse.data_ptr() if lse is not None else None
+    a.batch_heads, a.seq, a.head_dim = BH, N, D
+    a.causal = 1 if causal else 0
+    a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    _check(lib().gae_attn_int8_fwd(C.byref(a), _stream_ptr(stream)))
+    return (out, lse) if return_lse else out
+
+
+def int8_logits(q, k, stream=None):
+    """Exact int32 logits q @ k^T per (batch*head) through the tcgen05 int8 tiles."""
+    torch = _torch()
+    BH, Nq, D = q.shape
+    Nkv = k.shape[1]
+    out = torch.empty((BH, Nq, Nkv), dtype=torch.int32, device=q.device)
+    _check(lib().gae_int8_logits(q.contiguous().data_ptr(), k.contiguous().data_ptr(), BH, Nq,
+                                 Nkv, D, out.data_ptr(), _stream_ptr(stream)))
+    return out
+
+
+# ------------------------------------------------- host drop-ins of `ate`
+def _host_f32(x, n):
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32).reshape(-1))
+    if a.size < n:
+        # The crate indexes q[i*head_dim..] and panics on a short slice.
+        raise GAEError(1, f"input slice has {a.size} elements, need {n}")
+    return a
+
+
+def _host_call(fn, q, k, v, seq_len, head_dim, scale, causal):
+    n = seq_len * head_dim
+    qa, ka, va = (_host_f32(t, n) for t in (q, k, v))
+    out = np.empty(n, np.float32)
+    _check(fn(qa.ctypes.data, ka.ctypes.data, va.ctypes.data, seq_len, head_dim, scale,
+              1 if causal else 0, out.ctypes.data))
+    return out
+
+
+def waller_operator(q, k, v, seq_len: int, head_dim: int, scale: float, causal: bool = True):
+    """ate::waller_operator (rust_src/src/waller_operator.rs:8-15): causal fused
+    attention of one head, [seq_len, head_dim] fp32 row-major, on the GPU."""
+    return _host_call(lib().gae_waller_operator_f32_host, q, k, v, seq_len, head_dim, scale, causal)
+
+
+def waller_operator_parallel(q, k, v, seq_len: int, head_dim: int, scale: float,
+                             causal: bool = True):
+    """ate::waller_operator_parallel (rust_src/src/waller_operator.rs:63-70)."""
+    return _host_call(lib().gae_waller_operator_parallel_f32_host, q, k, v, seq_len, head_dim,
+                      scale, causal)
+
+
+def standard_attention(q, k, v, seq_len: int, head_dim: int, scale: float, causal: bool = True):
+    """ate::standard_attention (rust_src/src/standard_attention.rs:13-20)."""
+    return _host_call(lib().gae_standard_attention_f32_host, q, k, v, seq_len, head_dim, scale,
+                      causal)
+
+
+# ------------------------------------------ scalar helpers of the crate
+class OnlineSoftmax:
+    """ate::OnlineSoftmax (rust_src/src/online_softmax.rs:5-41)."""
+
+    def __init__(self):
+        self.max = float("-inf")
+        self.sum = 0.0
+
+    def update(self, score: float):
+        score = float(np.float32(score))
+        if score > self.max:
+            self.sum = float(np.float32(self.sum) * np.float32(math.exp(self.max - score)) + np.float32(1.0))
+            self.max = score
+        else:
+            self.sum = float(np.float32(self.sum) + np.float32(math.exp(score - self.max)))
+
+    def probability(self, score: float) -> float:
+        return float(np.float32(math.exp(score - self.max)) / np.float32(self.sum))
+
+
+class OnlineSoftmaxVec:
+    """ate::OnlineSoftmaxVec (rust_src/src/online_softmax.rs:44-68)."""
+
+    def __init__(self, n_heads: int):
+        self.states = [OnlineSoftmax() for _ in range(n_heads)]
+
+    def update(self, head: int, score: float):
+        self.states[head].update(score)
+
+    def reset(self):
+        self.states = [OnlineSoftmax() for _ in self.states]
+
+
+class WelfordState:
+    """ate::WelfordState (rust_src/src/welford.rs:5-55), f32 arithmetic."""
+
+    def __init__(self, mean=0.0, m2=0.0, count=0):
+        self.mean, self.m2, self.count = np.float32(mean), np.float32(m2), int(count)
+
+    def update(self, x: float):
+        x = np.float32(x)
+        self.count += 1
+        delta = x - self.mean
+        self.mean = self.mean + delta / np.float32(self.count)
+        self.m2 = self.m2 + delta * (x - self.mean)
+
+    def variance(self) -> float:
+        return 0.0 if self.count < 2 else float(self.m2 / np.float32(self.count))
+
+    def std(self, eps: float) -> float:
+        return float(np.sqrt(np.float32(self.variance()) + np.float32(eps)))
+
+    @staticmethod
+    def merge(a: "WelfordState", b: "WelfordState") -> "WelfordState":
+        count = a.count + b.count
+        if count == 0:
+            return WelfordState()
+        delta = b.mean - a.mean
+        mean = a.mean + delta * np.float32(b.count) / np.float32(count)
+        m2 = a.m2 + b.m2 + delta * delta * np.float32(a.count) * np.float32(b.count) / np.float32(count)
+        return WelfordState(mean, m2, count)
+
+
+def gelu(x: float) -> float:
+    """ate::gelu (rust_src/src/activations.rs:5-7), the tanh form."""
+    x = np.float32(x)
+    c = np.float32(math.sqrt(np.float32(2.0) / np.float32(math.pi)))
+    return float(np.float32(0.5) * x * (np.float32(1.0) + np.tanh(c * (x + np.float32(0.044715) * x * x * x))))
+
+
+def silu(x: float) -> float:
+    """ate::silu (rust_src/src/activations.rs:11-13)."""
+    x = np.float32(x)
+    return float(x / (np.float32(1.0) + np.float32(math.exp(-x))))
+
+
+def relu(x: float) -> float:
+    """ate::relu (rust_src/src/activations.rs:17-19)."""
+    return max(float(x), 0.0)
+
+
+@dataclass
+class GAEConfig:
+    """ate::GAEConfig (rust_src/src/config.rs:5-48)."""
+    hidden_dim: int
+    num_heads: int
+    head_dim: int
+    mlp_dim: int
+    ln_eps: float
+    max_seq_len: int
+
+    @classmethod
+    def new(cls, hidden_dim, num_heads, mlp_dim, max_seq_len):
+        if hidden_dim % num_heads != 0:
+            raise GAEError(1, "hidden_dim must be divisible by num_heads")
+        return cls(hidden_dim, num_heads, hidden_dim // num_heads, mlp_dim, 1e-5, max_seq_len)
+
+    @classmethod
+    def gpt2_small(cls):
+        return cls.new(768, 12, 3072, 1024)
+
+    @classmethod
+    def gpt2_medium(cls):
+        return cls.new(1024, 16, 4096, 1024)
+
+    @classmethod
+    def llama_7b(cls):
+        return cls.new(4096, 32, 11008, 4096)
+
+
+@dataclass
+class TransformerConfig:
+    """ate::TransformerConfig (rust_src/src/transformer.rs:9-33)."""
+    hidden_dim: int
+    num_heads: int
+    head_dim: int
+    mlp_dim: int
+    eps: float
+
+    @classmethod
+    def from_gae(cls, cfg: GAEConfig):
+        return cls(cfg.hidden_dim, cfg.num_heads, cfg.head_dim, cfg.mlp_dim, cfg.ln_eps)

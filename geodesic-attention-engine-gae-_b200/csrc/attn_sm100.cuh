@@ -1,0 +1,391 @@
+// attn_sm100.cuh -- fused exact attention forward for B200 (sm_100a) on the
+// 5th-generation tensor cores.
+//
+// Semantics: the reference's Waller operator (rust_src/src/waller_operator.rs
+// :8-59): O[i] = sum_j softmax_j(scale * <Q_i, K_j>) V_j, one streaming pass
+// over K/V with a running max and running sum per query row, no N x N
+// intermediate.  The reference's GPU versions are cuda_src/waller_kernel_bench
+// .cu:40-290 (cuBLAS tiles, S/P round-trip HBM) and cuda_src/bench_tma.cu:152-
+// 429 (Hopper TMA + wgmma); this kernel is a new design for tcgen05/TMEM.
+//
+// CTA = 256 query rows of one (batch, head): two 128-row Q tiles that
+// ping-pong on the tensor core.  Warp roles (320 threads):
+//   warps 0-3  softmax group 0  (Q tile 0, TMEM lanes 0..127, thread = row)
+//   warps 4-7  softmax group 1  (Q tile 1)
+//   warp  8    TMA producer     (Q once, then K_j, V_j into a smem ring)
+//   warp  9    MMA issuer       (owns the TMEM allocation)
+// TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 after it.
+// P_i (bf16, 2 per column) overwrites the first 64 columns of S_i and feeds
+// the P*V MMA straight from TMEM.  Per K/V tile j the MMA warp issues
+//   PV0(j-1), QK0(j), PV1(j-1), QK1(j)
+// so S_i is rewritten only after the MMA that read P_i was issued (tcgen05
+// MMAs of one thread execute in issue order), and the commit that publishes
+// S_i(j) also proves PV_i(j-1) finished, which lets softmax group i rescale
+// O_i without another barrier.
+//
+// Softmax works in the log2 domain with lazy rescaling: the running max used
+// as exponent base moves only when a row max exceeds it by more than 8
+// (2^8 headroom), which is exact because the final 1/l uses the same base.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace gae {
+
+struct AttnParams {
+    CUtensorMap tm_q;  // dims {D, Nq, H, B}, box {64, 128, 1, 1}, 128B swizzle
+    CUtensorMap tm_k;  // dims {D, Nkv, H, B}
+    CUtensorMap tm_v;
+    void *o;
+    float *lse;
+    int64_t o_sb, o_sh, o_ss;  // element strides of O
+    int B, H, Nq, Nkv;
+    int n_qpairs;
+    int causal;
+    float scale_log2;  // scale * log2(e)
+    int64_t q_offset, kv_offset;
+};
+
+enum AttnWaitSite : unsigned {
+    kSiteQ = 0x101,
+    kSiteKvFull = 0x102,
+    kSiteKvEmpty = 0x103,
+    kSiteS = 0x104,
+    kSiteP = 0x105,
+    kSiteO = 0x106,
+    kSiteDone = 0x107,
+};
+
+template <int D>
+struct AttnCfg {
+    static constexpr int kBlockM = 128;                  // rows per Q tile
+    static constexpr int kBlockN = 128;                  // keys per K/V tile
+    static constexpr int kHalves = D / 64;               // 128-byte swizzle boxes per row
+    static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 128 B
+    static constexpr int kTileBytes = kHalves * kBoxBytes;
+    static constexpr int kStages = (D == 128) ? 4 : 8;   // K/V ring slots
+    static constexpr int kQBytes = 2 * kTileBytes;
+    static constexpr int kRingBytes = kStages * kTileBytes;
+    static constexpr int kBarOffset = kQBytes + kRingBytes;
+    // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done
+    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
+    static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
+    static constexpr uint32_t kTmemCols = 512;
+    static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
+    static constexpr int kThreads = 320;
+};
+
+template <int D, bool kBF16>
+__global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
+    using Cfg = AttnCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the 128B-swizzle atoms.
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base - raw_addr);
+
+    const uint32_t sQ = base;
+    const uint32_t sRing = base + Cfg::kQBytes;
+    const uint32_t sBar = base + Cfg::kBarOffset;
+    auto bar_q = [&]() { return sBar; };
+    auto bar_kv_full = [&](int s) { return sBar + 8u * (1 + s); };
+    auto bar_kv_empty = [&](int s) { return sBar + 8u * (1 + Cfg::kStages + s); };
+    auto bar_s = [&](int i) { return sBar + 8u * (1 + 2 * Cfg::kStages + i); };
+    auto bar_p = [&](int i) { return sBar + 8u * (3 + 2 * Cfg::kStages + i); };
+    auto bar_o = [&](int i) { return sBar + 8u * (5 + 2 * Cfg::kStages + i); };
+    const uint32_t bar_done = sBar + 8u * (7 + 2 * Cfg::kStages);
+    uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kBarOffset + Cfg::kNumBars * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
+
+    volatile int no_abort = 0;  // for drains that must not be cut short
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    const int qpair = p.n_qpairs - 1 - (int)blockIdx.x;  // heaviest (causal) first
+    const int bh = blockIdx.y;
+    const int b = bh / p.H, h = bh % p.H;
+    const int q0 = qpair * 256;
+
+    // Number of K/V tiles this CTA visits.
+    int n_kv = (p.Nkv + Cfg::kBlockN - 1) / Cfg::kBlockN;
+    if (p.causal) {
+        const int64_t last_q = p.q_offset + (int64_t)min(q0 + 255, p.Nq - 1);
+        const int64_t last_key = last_q - p.kv_offset;
+        if (last_key < 0) n_kv = 0;
+        else n_kv = (int)min64((int64_t)n_kv, last_key / Cfg::kBlockN + 1);
+    }
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_q(), 1);
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(bar_kv_full(s), 1);
+            mbar_init(bar_kv_empty(s), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar_s(i), 1);
+            mbar_init(bar_p(i), 128);
+            mbar_init(bar_o(i), 1);
+        }
+        mbar_init(bar_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 9 && n_kv > 0) {
+        tmem_alloc(smem_u32(tmem_base_slot), Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = (n_kv > 0) ? *tmem_base_slot : 0u;
+
+    if (warp == 8) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0 && n_kv > 0) {
+            tma_prefetch_desc(&p.tm_q);
+            tma_prefetch_desc(&p.tm_k);
+            tma_prefetch_desc(&p.tm_v);
+            mbar_expect_tx(bar_q(), Cfg::kQBytes);
+            for (int t = 0; t < 2; ++t)
+                for (int hf = 0; hf < Cfg::kHalves; ++hf)
+                    tma_load_4d(sQ + t * Cfg::kTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
+                                hf * 64, q0 + t * 128, h, b);
+            bool ok = true;
+            int issued = 0;
+            for (int j = 0; j < n_kv && ok; ++j) {
+                for (int kv = 0; kv < 2 && ok; ++kv) {
+                    const int item = 2 * j + kv;
+                    const int slot = item % Cfg::kStages;
+                    const int use = item / Cfg::kStages;
+                    if (use > 0) ok = mbar_wait(bar_kv_empty(slot), (use - 1) & 1, kSiteKvEmpty, abort_flag);
+                    if (!ok) break;
+                    const uint32_t dst = sRing + slot * Cfg::kTileBytes;
+                    const CUtensorMap *m = kv ? &p.tm_v : &p.tm_k;
+                    mbar_expect_tx(bar_kv_full(slot), Cfg::kTileBytes);
+                    for (int hf = 0; hf < Cfg::kHalves; ++hf)
+                        tma_load_4d(dst + hf * Cfg::kBoxBytes, m, bar_kv_full(slot), hf * 64,
+                                    j * Cfg::kBlockN, h, b);
+                    issued = item + 1;
+                }
+            }
+            // Drain: the last copy issued into each slot has landed before the
+            // CTA can exit (bounded; normally already complete).
+            mbar_wait(bar_q(), 0, kSiteQ, &no_abort);
+            for (int item = max(0, issued - Cfg::kStages); item < issued; ++item)
+                mbar_wait(bar_kv_full(item % Cfg::kStages), (item / Cfg::kStages) & 1, kSiteKvFull,
+                          &no_abort);
+        }
+    } else if (warp == 9) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0 && n_kv > 0) {
+            constexpr uint32_t idesc_qk = idesc_f16(128, 128, kBF16, false, false);
+            constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, false, true);
+            bool ok = mbar_wait(bar_q(), 0, kSiteQ, abort_flag);
+            auto issue_qk = [&](int i, int slot) {
+                const uint32_t d_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
+                const uint32_t qa = sQ + i * Cfg::kTileBytes;
+                const uint32_t kb = sRing + slot * Cfg::kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32;
+                    umma_f16_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024),
+                                smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+                }
+            };
+            auto issue_pv = [&](int i, int slot, bool acc) {
+                const uint32_t d_tmem = tmem + (i ? Cfg::kColO1 : Cfg::kColO0);
+                const uint32_t p_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
+                const uint32_t vb = sRing + slot * Cfg::kTileBytes;
+#pragma unroll
+                for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk) {
+                    umma_f16_ts(d_tmem, p_tmem + kk * 8,
+                                smem_desc_sw128(vb + kk * 16 * 128, Cfg::kBoxBytes, 1024), idesc_pv,
+                                (acc || kk > 0) ? 1u : 0u);
+                }
+            };
+            for (int j = 0; j < n_kv && ok; ++j) {
+                const int k_item = 2 * j, k_slot = k_item % Cfg::kStages;
+                const int v_item = 2 * j - 1, v_slot = (v_item + Cfg::kStages) % Cfg::kStages;
+                ok = mbar_wait(bar_kv_full(k_slot), (k_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag);
+                if (!ok) break;
+                if (j > 0) {
+                    ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
+                         mbar_wait(bar_p(0), (j - 1) & 1, kSiteP, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(0, v_slot, j - 1 > 0);
+                }
+                issue_qk(0, k_slot);
+                umma_commit(bar_s(0));
+                if (j > 0) {
+                    ok = mbar_wait(bar_p(1), (j - 1) & 1, kSiteP, abort_flag);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(1, v_slot, j - 1 > 0);
+                    umma_commit(bar_kv_empty(v_slot));
+                }
+                issue_qk(1, k_slot);
+                umma_commit(bar_s(1));
+                umma_commit(bar_kv_empty(k_slot));
+            }
+            if (ok) {
+                const int v_item = 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
+                ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
+                     mbar_wait(bar_p(0), (n_kv - 1) & 1, kSiteP, abort_flag);
+                if (ok) {
+                    tc_fence_after();
+                    issue_pv(0, v_slot, n_kv > 1);
+                    umma_commit(bar_o(0));
+                    ok = mbar_wait(bar_p(1), (n_kv - 1) & 1, kSiteP, abort_flag);
+                }
+                if (ok) {
+                    tc_fence_after();
+                    issue_pv(1, v_slot, n_kv > 1);
+                    umma_commit(bar_o(1));
+                    umma_commit(bar_kv_empty(v_slot));
+                }
+            }
+            // Drain: every MMA this thread issued has completed before TMEM is
+            // freed (bounded, and not cut short by the abort flag).
+            umma_commit(bar_done);
+            mbar_wait(bar_done, 0, kSiteDone, &no_abort);
+        }
+    } else {
+        // ------------------------------------------------------ softmax groups
+        const int grp = warp >> 2;       // Q tile 0 or 1
+        const int wq = warp & 3;         // TMEM lane quarter
+        const int row = wq * 32 + lane;  // row within the Q tile
+        const int q_local = q0 + grp * 128 + row;
+        const int64_t q_abs = p.q_offset + q_local;
+        const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
+        const uint32_t tS = tmem + lane_off + (grp ? Cfg::kColS1 : Cfg::kColS0);
+        const uint32_t tO = tmem + lane_off + (grp ? Cfg::kColO1 : Cfg::kColO0);
+        const float sl2 = p.scale_log2;
+
+        float m_run = -INFINITY;  // exponent base, log2 domain (scaled)
+        float l_run = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_kv; ++j) {
+            ok = mbar_wait(bar_s(grp), j & 1, kSiteS, abort_flag);
+            if (!ok) break;
+            tc_fence_after();
+            float s[128];
+            {
+                uint32_t r0[32], r1[32], r2[32], r3[32];
+                tmem_ld32(tS + 0, r0);
+                tmem_ld32(tS + 32, r1);
+                tmem_ld32(tS + 64, r2);
+                tmem_ld32(tS + 96, r3);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    s[e] = __uint_as_float(r0[e]);
+                    s[32 + e] = __uint_as_float(r1[e]);
+                    s[64 + e] = __uint_as_float(r2[e]);
+                    s[96 + e] = __uint_as_float(r3[e]);
+                }
+            }
+            // Masking: causal boundary and the ragged end of the key range.
+            const int64_t k_abs0 = p.kv_offset + (int64_t)j * Cfg::kBlockN;
+            int limit = min(Cfg::kBlockN, p.Nkv - j * Cfg::kBlockN);
+            if (p.causal) {
+                const int64_t lim_c = q_abs - k_abs0 + 1;
+                if (lim_c < limit) limit = (int)max64(lim_c, 0);
+            }
+            if (limit < Cfg::kBlockN) {
+#pragma unroll
+                for (int c = 0; c < 128; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
+            const float m_tile = mx * sl2;
+            float alpha = 1.f;
+            if (m_tile > m_run + 8.f) {  // also true while m_run == -inf and the tile sees a key
+                alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_tile);
+                m_run = m_tile;
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+            float rs = 0.f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = ex2_approx(fmaf(s[c * 32 + 2 * e], sl2, -m_use));
+                    const float p1 = ex2_approx(fmaf(s[c * 32 + 2 * e + 1], sl2, -m_use));
+                    rs += p0 + p1;
+                    pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+                }
+                tmem_st16(tS + c * 16, pk);
+            }
+            l_run = l_run * alpha + rs;
+            // Rescale O_i when the base moved (warp-uniform: tcgen05.ld/st are
+            // warp-collective).  PV_i(j-1) has completed: its commit preceded S_i(j)'s.
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld32(tO + c * 32, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                    tmem_st32(tO + c * 32, r);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(bar_p(grp));
+        }
+
+        // Epilogue: O_i / l -> global; log-sum-exp.
+        const bool row_valid = q_local < p.Nq;
+        const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+        if (n_kv > 0 && ok) ok = mbar_wait(bar_o(grp), 0, kSiteO, abort_flag);
+        if (n_kv > 0 && ok) {
+            tc_fence_after();
+            char *orow = reinterpret_cast<char *>(p.o) +
+                         2 * (b * p.o_sb + h * p.o_sh + (int64_t)q_local * p.o_ss);
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tO + c * 32, r);
+                tmem_wait_ld();
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float a0 = __uint_as_float(r[2 * e]) * inv_l;
+                    const float a1 = __uint_as_float(r[2 * e + 1]) * inv_l;
+                    pk[e] = kBF16 ? pack_bf16x2(a0, a1) : pack_f16x2(a0, a1);
+                }
+                if (row_valid) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(orow + c * 64);
+#pragma unroll
+                    for (int v = 0; v < 4; ++v)
+                        dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                }
+            }
+        } else if (n_kv == 0 && row_valid) {
+            char *orow = reinterpret_cast<char *>(p.o) +
+                         2 * (b * p.o_sb + h * p.o_sh + (int64_t)q_local * p.o_ss);
+            for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4 *>(orow)[c] = make_uint4(0, 0, 0, 0);
+        }
+        if (p.lse && row_valid) {
+            float lse = -INFINITY;
+            if (l_run > 0.f) lse = (m_run + __log2f(l_run)) * 0.69314718055994531f;
+            p.lse[(int64_t)bh * p.Nq + q_local] = lse;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9 && n_kv > 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+}
+
+}  // namespace gae

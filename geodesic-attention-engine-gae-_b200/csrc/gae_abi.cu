@@ -1,0 +1,405 @@
+// gae_abi.cu -- the C ABI of libgae.so (declared in include/gae.h).
+//
+// This translation unit owns argument validation, error reporting, TMA
+// descriptor encoding and kernel launches.  The kernels live in the headers
+// it includes (one translation unit, so that the device-side error record
+// gae_dev_error is a single symbol without relocatable device code).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/gae.h"
+#include "attn_f32.cuh"
+#include "attn_sm100.cuh"
+#include "attn_int8_sm100.cuh"
+#include "layer_sm100.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+thread_local gae_status g_err_status = GAE_OK;
+
+gae_status fail(gae_status s, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    g_err_status = s;
+    return s;
+}
+
+#define GAE_CUDA_TRY(expr)                                                                 \
+    do {                                                                                   \
+        cudaError_t e_ = (expr);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            return fail(e_ == cudaErrorMemoryAllocation ? GAE_ERR_OOM : GAE_ERR_CUDA,     \
+                        "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, \
+                        __LINE__);                                                         \
+    } while (0)
+
+// ---------------------------------------------------------------- TMA maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 4-D map over a [B, H, N, D] view with element strides {sb, sh, ss, 1},
+// box {64 elements (128 B), box_rows, 1, 1}, 128-byte swizzle.
+gae_status make_map_4d(CUtensorMap *m, const void *ptr, CUtensorMapDataType dt, int esize,
+                       int64_t B, int64_t H, int64_t N, int64_t D, int64_t sb, int64_t sh,
+                       int64_t ss, int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)N, (cuuint64_t)H, (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)(ss * esize), (cuuint64_t)(sh * esize),
+                             (cuuint64_t)(sb * esize)};
+    cuuint32_t box[4] = {(cuuint32_t)(128 / esize), (cuuint32_t)box_rows, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, dt, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GAE_OK;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename Kern>
+gae_status set_smem(Kern k, int bytes) {
+    GAE_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    return GAE_OK;
+}
+
+// ------------------------------------------------------------ attention
+gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
+    const bool bf16 = a->dtype == GAE_DTYPE_BF16;
+    const int64_t D = a->head_dim;
+    if (D != 64 && D != 128)
+        return fail(GAE_ERR_UNSUPPORTED, "tensor-core attention supports head_dim 64 or 128, got %lld",
+                    (long long)D);
+    const void *ptrs[4] = {a->q, a->k, a->v, a->o};
+    for (const void *pp : ptrs)
+        if (!aligned16(pp)) return fail(GAE_ERR_INVALID_ARG, "q/k/v/o must be 16-byte aligned");
+    const int64_t *strs[4] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride};
+    for (const int64_t *s : strs)
+        for (int i = 0; i < 3; ++i)
+            if (s[i] < 0 || (s[i] % 8) != 0)
+                return fail(GAE_ERR_INVALID_ARG,
+                            "strides must be non-negative multiples of 8 elements (16 bytes)");
+    if (a->batch * a->heads > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch*heads > 65535");
+    if (a->seq_q > (1ll << 30) || a->seq_kv > (1ll << 30))
+        return fail(GAE_ERR_UNSUPPORTED, "sequence longer than 2^30");
+
+    gae::AttnParams p;
+    memset(&p, 0, sizeof(p));
+    const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    gae_status s;
+    if ((s = make_map_4d(&p.tm_q, a->q, dt, 2, a->batch, a->heads, a->seq_q, D, a->q_stride[0],
+                         a->q_stride[1], a->q_stride[2], 128)) != GAE_OK)
+        return s;
+    if ((s = make_map_4d(&p.tm_k, a->k, dt, 2, a->batch, a->heads, a->seq_kv, D, a->k_stride[0],
+                         a->k_stride[1], a->k_stride[2], 128)) != GAE_OK)
+        return s;
+    if ((s = make_map_4d(&p.tm_v, a->v, dt, 2, a->batch, a->heads, a->seq_kv, D, a->v_stride[0],
+                         a->v_stride[1], a->v_stride[2], 128)) != GAE_OK)
+        return s;
+    p.o = a->o;
+    p.lse = a->lse;
+    p.o_sb = a->o_stride[0];
+    p.o_sh = a->o_stride[1];
+    p.o_ss = a->o_stride[2];
+    p.B = (int)a->batch;
+    p.H = (int)a->heads;
+    p.Nq = (int)a->seq_q;
+    p.Nkv = (int)a->seq_kv;
+    p.n_qpairs = (int)((a->seq_q + 255) / 256);
+    p.causal = a->causal ? 1 : 0;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    p.q_offset = a->q_offset;
+    p.kv_offset = a->kv_offset;
+    dim3 grid(p.n_qpairs, (unsigned)(a->batch * a->heads));
+
+#define GAE_LAUNCH_TC(DD, BF)                                                              \
+    do {                                                                                   \
+        auto kern = gae::attn_fwd_sm100_kernel<DD, BF>;                                    \
+        constexpr int smem = gae::AttnCfg<DD>::kSmemBytes;                                 \
+        if ((s = set_smem(kern, smem)) != GAE_OK) return s;                                \
+        kern<<<grid, gae::AttnCfg<DD>::kThreads, smem, st>>>(p);                           \
+    } while (0)
+    if (D == 128) {
+        if (bf16) GAE_LAUNCH_TC(128, true); else GAE_LAUNCH_TC(128, false);
+    } else {
+        if (bf16) GAE_LAUNCH_TC(64, true); else GAE_LAUNCH_TC(64, false);
+    }
+#undef GAE_LAUNCH_TC
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status launch_attn_f32(const gae_attn_args *a, cudaStream_t st) {
+    const int64_t D = a->head_dim;
+    if (D > 256) return fail(GAE_ERR_UNSUPPORTED, "fp32 attention supports head_dim <= 256");
+    gae::AttnF32Params p;
+    p.q = static_cast<const float *>(a->q);
+    p.k = static_cast<const float *>(a->k);
+    p.v = static_cast<const float *>(a->v);
+    p.o = static_cast<float *>(a->o);
+    p.lse = a->lse;
+    p.q_sb = a->q_stride[0]; p.q_sh = a->q_stride[1]; p.q_ss = a->q_stride[2];
+    p.k_sb = a->k_stride[0]; p.k_sh = a->k_stride[1]; p.k_ss = a->k_stride[2];
+    p.v_sb = a->v_stride[0]; p.v_sh = a->v_stride[1]; p.v_ss = a->v_stride[2];
+    p.o_sb = a->o_stride[0]; p.o_sh = a->o_stride[1]; p.o_ss = a->o_stride[2];
+    p.B = (int)a->batch; p.H = (int)a->heads; p.Nq = (int)a->seq_q; p.Nkv = (int)a->seq_kv;
+    p.D = (int)D;
+    p.causal = a->causal ? 1 : 0;
+    p.scale = a->scale;
+    p.q_offset = a->q_offset;
+    p.kv_offset = a->kv_offset;
+    if (a->batch * a->heads > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch*heads > 65535");
+    dim3 grid((unsigned)((a->seq_q + gae::kF32Rows - 1) / gae::kF32Rows),
+              (unsigned)(a->batch * a->heads));
+    gae_status s;
+#define GAE_LAUNCH_F32(DM)                                                                   \
+    do {                                                                                     \
+        constexpr int smem = (DM * gae::kF32Rows + 2 * gae::kF32Keys * DM) * 4;              \
+        if ((s = set_smem(gae::attn_fwd_f32_kernel<DM>, smem)) != GAE_OK) return s;         \
+        gae::attn_fwd_f32_kernel<DM><<<grid, gae::kF32Rows, smem, st>>>(p);                 \
+    } while (0)
+    if (D <= 32) GAE_LAUNCH_F32(32);
+    else if (D <= 64) GAE_LAUNCH_F32(64);
+    else if (D <= 128) GAE_LAUNCH_F32(128);
+    else GAE_LAUNCH_F32(256);
+#undef GAE_LAUNCH_F32
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status check_attn_args(const gae_attn_args *a) {
+    if (!a) return fail(GAE_ERR_INVALID_ARG, "args is NULL");
+    if (a->batch < 1 || a->heads < 1 || a->seq_q < 0 || a->seq_kv < 0 || a->head_dim < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid shape B=%lld H=%lld Nq=%lld Nkv=%lld D=%lld",
+                    (long long)a->batch, (long long)a->heads, (long long)a->seq_q,
+                    (long long)a->seq_kv, (long long)a->head_dim);
+    if (a->seq_q > 0 && (!a->q || !a->o))
+        return fail(GAE_ERR_INVALID_ARG, "q/o pointers are NULL");
+    if (a->seq_kv > 0 && (!a->k || !a->v))
+        return fail(GAE_ERR_INVALID_ARG, "k/v pointers are NULL");
+    if (!(a->scale == a->scale)) return fail(GAE_ERR_INVALID_ARG, "scale is NaN");
+    return GAE_OK;
+}
+
+gae_status host_attention(const float *q, const float *k, const float *v, size_t n, size_t d,
+                          float scale, int causal, float *out) {
+    if (n == 0) return GAE_OK;
+    if (!q || !k || !v || !out) return fail(GAE_ERR_INVALID_ARG, "NULL host pointer");
+    if (d == 0 || d > 256) return fail(GAE_ERR_UNSUPPORTED, "head_dim must be in [1, 256]");
+    const size_t bytes = n * d * sizeof(float);
+    float *dq = nullptr, *dk = nullptr, *dv = nullptr, *dout = nullptr;
+    gae_status s = GAE_OK;
+    cudaStream_t st = nullptr;
+    auto cleanup = [&] {
+        if (dq) cudaFree(dq);
+        if (dk) cudaFree(dk);
+        if (dv) cudaFree(dv);
+        if (dout) cudaFree(dout);
+        if (st) cudaStreamDestroy(st);
+    };
+    do {
+        cudaError_t e;
+        if ((e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaMalloc(&dq, bytes)) != cudaSuccess || (e = cudaMalloc(&dk, bytes)) != cudaSuccess ||
+            (e = cudaMalloc(&dv, bytes)) != cudaSuccess || (e = cudaMalloc(&dout, bytes)) != cudaSuccess) {
+            s = fail(e == cudaErrorMemoryAllocation ? GAE_ERR_OOM : GAE_ERR_CUDA,
+                     "device setup failed: %s", cudaGetErrorString(e));
+            break;
+        }
+        if ((e = cudaMemcpyAsync(dq, q, bytes, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(dk, k, bytes, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+            (e = cudaMemcpyAsync(dv, v, bytes, cudaMemcpyHostToDevice, st)) != cudaSuccess) {
+            s = fail(GAE_ERR_CUDA, "H2D copy failed: %s", cudaGetErrorString(e));
+            break;
+        }
+        gae_attn_args a;
+        memset(&a, 0, sizeof(a));
+        a.q = dq; a.k = dk; a.v = dv; a.o = dout;
+        a.batch = 1; a.heads = 1; a.seq_q = (int64_t)n; a.seq_kv = (int64_t)n; a.head_dim = (int64_t)d;
+        const int64_t st3[3] = {(int64_t)(n * d), (int64_t)(n * d), (int64_t)d};
+        memcpy(a.q_stride, st3, sizeof st3); memcpy(a.k_stride, st3, sizeof st3);
+        memcpy(a.v_stride, st3, sizeof st3); memcpy(a.o_stride, st3, sizeof st3);
+        a.dtype = GAE_DTYPE_F32;
+        a.causal = causal;
+        a.scale = scale;
+        if ((s = launch_attn_f32(&a, st)) != GAE_OK) break;
+        if ((e = cudaMemcpyAsync(out, dout, bytes, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+            (e = cudaStreamSynchronize(st)) != cudaSuccess) {
+            s = fail(GAE_ERR_CUDA, "kernel or D2H copy failed: %s", cudaGetErrorString(e));
+            break;
+        }
+    } while (0);
+    cleanup();
+    return s;
+}
+
+}  // namespace
+
+// ==================================================================== C ABI
+extern "C" {
+
+const char *gae_status_string(gae_status s) {
+    switch (s) {
+        case GAE_OK: return "GAE_OK";
+        case GAE_ERR_INVALID_ARG: return "GAE_ERR_INVALID_ARG";
+        case GAE_ERR_UNSUPPORTED: return "GAE_ERR_UNSUPPORTED";
+        case GAE_ERR_CUDA: return "GAE_ERR_CUDA";
+        case GAE_ERR_OOM: return "GAE_ERR_OOM";
+        case GAE_ERR_COMM: return "GAE_ERR_COMM";
+        case GAE_ERR_TIMEOUT: return "GAE_ERR_TIMEOUT";
+    }
+    return "GAE_ERR_UNKNOWN";
+}
+
+gae_status gae_last_error(char *buf, size_t n) {
+    if (buf && n) {
+        strncpy(buf, g_err, n - 1);
+        buf[n - 1] = '\0';
+    }
+    return g_err_status;
+}
+
+const char *gae_version(void) { return "0.1.0"; }
+
+gae_status gae_device_status(int reset) {
+    GAE_CUDA_TRY(cudaDeviceSynchronize());
+    unsigned v = 0;
+    GAE_CUDA_TRY(cudaMemcpyFromSymbol(&v, gae::gae_dev_error, sizeof(v)));
+    if (reset) {
+        unsigned z = 0;
+        GAE_CUDA_TRY(cudaMemcpyToSymbol(gae::gae_dev_error, &z, sizeof(z)));
+    }
+    if (v) return fail(GAE_ERR_TIMEOUT, "a device-side wait timed out (site 0x%x)", v);
+    return GAE_OK;
+}
+
+gae_status gae_waller_operator_f32_host(const float *q, const float *k, const float *v,
+                                        size_t seq_len, size_t head_dim, float scale, int causal,
+                                        float *out) {
+    return host_attention(q, k, v, seq_len, head_dim, scale, causal, out);
+}
+
+gae_status gae_waller_operator_parallel_f32_host(const float *q, const float *k, const float *v,
+                                                 size_t seq_len, size_t head_dim, float scale,
+                                                 int causal, float *out) {
+    return host_attention(q, k, v, seq_len, head_dim, scale, causal, out);
+}
+
+gae_status gae_standard_attention_f32_host(const float *q, const float *k, const float *v,
+                                           size_t seq_len, size_t head_dim, float scale,
+                                           int causal, float *out) {
+    return host_attention(q, k, v, seq_len, head_dim, scale, causal, out);
+}
+
+gae_status gae_attn_fwd(const gae_attn_args *a, void *stream) {
+    gae_status s = check_attn_args(a);
+    if (s != GAE_OK) return s;
+    if (a->seq_q == 0) return GAE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    switch (a->dtype) {
+        case GAE_DTYPE_F32: return launch_attn_f32(a, st);
+        case GAE_DTYPE_BF16:
+        case GAE_DTYPE_F16: return launch_attn_tc(a, st);
+    }
+    return fail(GAE_ERR_INVALID_ARG, "unknown dtype %d", (int)a->dtype);
+}
+
+gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part, const float *lse_part,
+                         int64_t rows, int64_t head_dim, int64_t sa, int64_t sp, gae_dtype dtype,
+                         void *stream) {
+    if (rows == 0) return GAE_OK;
+    if (!o_acc || !lse_acc || !o_part || !lse_part || rows < 0 || head_dim < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid lse_merge arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int warps = 8;
+    dim3 grid((unsigned)((rows + warps - 1) / warps));
+    switch (dtype) {
+        case GAE_DTYPE_F32:
+            gae::lse_merge_kernel<float><<<grid, warps * 32, 0, st>>>(
+                (float *)o_acc, lse_acc, (const float *)o_part, lse_part, rows, (int)head_dim, sa, sp);
+            break;
+        case GAE_DTYPE_BF16:
+            gae::lse_merge_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(
+                (__nv_bfloat16 *)o_acc, lse_acc, (const __nv_bfloat16 *)o_part, lse_part, rows,
+                (int)head_dim, sa, sp);
+            break;
+        case GAE_DTYPE_F16:
+            gae::lse_merge_kernel<__half><<<grid, warps * 32, 0, st>>>(
+                (__half *)o_acc, lse_acc, (const __half *)o_part, lse_part, rows, (int)head_dim, sa, sp);
+            break;
+        default: return fail(GAE_ERR_INVALID_ARG, "unknown dtype");
+    }
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, int64_t d,
+                                  int8_t *q, float *scale, void *stream) {
+    if (rows == 0) return GAE_OK;
+    if (!x || !q || !scale || rows < 0 || d < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid quantize arguments");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int warps = 8;
+    dim3 grid((unsigned)((rows + warps - 1) / warps));
+    if (dtype == GAE_DTYPE_F32)
+        gae::quantize_rows_int8_kernel<float><<<grid, warps * 32, 0, st>>>((const float *)x, rows, (int)d, q, scale);
+    else if (dtype == GAE_DTYPE_BF16)
+        gae::quantize_rows_int8_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(
+            (const __nv_bfloat16 *)x, rows, (int)d, q, scale);
+    else
+        return fail(GAE_ERR_UNSUPPORTED, "quantize supports f32 and bf16 input");
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------
+// Entry points whose kernels are not in this build yet: they validate nothing
+// and report GAE_ERR_UNSUPPORTED so that a caller fails loudly.
+extern "C" {
+gae_status gae_attn_int8_fwd(const gae_attn_int8_args *, void *) {
+    return fail(GAE_ERR_UNSUPPORTED, "gae_attn_int8_fwd: not built");
+}
+gae_status gae_int8_logits(const int8_t *, const int8_t *, int64_t, int64_t, int64_t, int64_t,
+                           int32_t *, void *) {
+    return fail(GAE_ERR_UNSUPPORTED, "gae_int8_logits: not built");
+}
+size_t gae_layer_workspace_bytes(int64_t, int64_t, int64_t, int64_t) { return 0; }
+gae_status gae_layer_fwd(const gae_layer_args *, const gae_layer_weights *, void *) {
+    return fail(GAE_ERR_UNSUPPORTED, "gae_layer_fwd: not built");
+}
+gae_status gae_layer_stack_fwd(const gae_layer_args *, const gae_layer_weights *, int, void *) {
+    return fail(GAE_ERR_UNSUPPORTED, "gae_layer_stack_fwd: not built");
+}
+gae_status gae_layernorm_fwd(const void *, const void *, void *, void *, const float *,
+                             const float *, int64_t, int64_t, float, void *) {
+    return fail(GAE_ERR_UNSUPPORTED, "gae_layernorm_fwd: not built");
+}
+}

@@ -1,0 +1,241 @@
+/*
+ * gae.h -- C ABI of the gae-b200 library (libgae.so): the Geodesic Attention
+ * Engine's fused "Waller" attention path, rebuilt for NVIDIA B200 (sm_100a).
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, never
+ * throws or exits, and returns a gae_status.  On failure a thread-local detail
+ * string is available from gae_last_error().  Entry points that take a
+ * `stream` are asynchronous with respect to the host and ordered on that CUDA
+ * stream (pass a cudaStream_t cast to void*, or NULL for the legacy default
+ * stream).  The *_host entry points take host memory and are synchronous.
+ *
+ * Each declaration names the reference interface it replaces
+ * (RegularJoe-CEO/Geodesic-Attention-Engine-GAE-, path:line inside that
+ * project).  The reference crate `ate` panics on bad input; the Rust binding
+ * shown in INTEGRATION.md turns a non-GAE_OK status back into a panic.
+ */
+#ifndef GAE_H_
+#define GAE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GAE_API __attribute__((visibility("default")))
+#else
+#define GAE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    GAE_OK = 0,
+    GAE_ERR_INVALID_ARG = 1,  /* bad shape, stride, alignment or pointer      */
+    GAE_ERR_UNSUPPORTED = 2,  /* valid request this build has no kernel for   */
+    GAE_ERR_CUDA = 3,         /* a CUDA runtime/driver call failed            */
+    GAE_ERR_OOM = 4,          /* device allocation failed (host entry points) */
+    GAE_ERR_COMM = 5,         /* ring transport failure                       */
+    GAE_ERR_TIMEOUT = 6       /* a bounded device-side wait gave up           */
+} gae_status;
+
+typedef enum {
+    GAE_DTYPE_F32 = 0,
+    GAE_DTYPE_BF16 = 1,
+    GAE_DTYPE_F16 = 2
+} gae_dtype;
+
+/* Human-readable name of a status code (static string). */
+GAE_API const char *gae_status_string(gae_status s);
+
+/* Copies the calling thread's last error detail into buf (NUL-terminated,
+ * truncated to n bytes) and returns the status it was recorded with. */
+GAE_API gae_status gae_last_error(char *buf, size_t n);
+
+/* Library version, "major.minor.patch". */
+GAE_API const char *gae_version(void);
+
+/* Synchronises the current device and reports whether any kernel of this
+ * library recorded a device-side failure (a bounded wait that ran out) since
+ * the last reset.  reset != 0 clears the record.  GAE_OK or GAE_ERR_TIMEOUT. */
+GAE_API gae_status gae_device_status(int reset);
+
+/* ------------------------------------------------------------------------
+ * Host-memory drop-ins for the Rust crate's attention functions.
+ * Layout as in the reference: q, k, v, out are [seq_len, head_dim] fp32
+ * row-major, one head.  Computes out[i] = sum_j softmax_j(scale*<q_i,k_j>) v_j
+ * over j <= i (causal != 0, the reference's only mode) or over all j
+ * (causal == 0).  fp32 CUDA-core kernel, fp32 throughout.  head_dim <= 256.
+ * ---------------------------------------------------------------------- */
+
+/* replaces ate::waller_operator, rust_src/src/waller_operator.rs:8-15 */
+GAE_API gae_status gae_waller_operator_f32_host(const float *q, const float *k, const float *v,
+                                        size_t seq_len, size_t head_dim, float scale,
+                                        int causal, float *out);
+
+/* replaces ate::waller_operator_parallel, rust_src/src/waller_operator.rs:63-70
+ * (same result; the GPU runs all rows in parallel either way) */
+GAE_API gae_status gae_waller_operator_parallel_f32_host(const float *q, const float *k,
+                                                 const float *v, size_t seq_len,
+                                                 size_t head_dim, float scale, int causal,
+                                                 float *out);
+
+/* replaces ate::standard_attention, rust_src/src/standard_attention.rs:13-20.
+ * The reference materialises the N x N scores; this entry point returns the
+ * same softmax attention through the fused streaming kernel (no N x N
+ * buffer), which the reference's own test pins as equal within 1e-4
+ * (tests/validation.rs:147-163). */
+GAE_API gae_status gae_standard_attention_f32_host(const float *q, const float *k, const float *v,
+                                           size_t seq_len, size_t head_dim, float scale,
+                                           int causal, float *out);
+
+/* ------------------------------------------------------------------------
+ * Device-pointer attention (the reference's CUDA Waller kernels:
+ * cuda_src/waller_operator.cu:12-100 fp32, cuda_src/waller_kernel_bench.cu:
+ * 164-290 fp16 tiles, cuda_src/bench_tma.cu:152-429 TMA/wgmma).
+ *
+ * Q [batch, heads, seq_q, head_dim], K/V [batch, heads, seq_kv, head_dim],
+ * O like Q, addressed through element strides {batch, head, seq}; the
+ * head_dim stride is 1.  lse (optional, fp32, contiguous [batch, heads,
+ * seq_q]) receives the natural-log log-sum-exp of each row's scaled scores,
+ * -inf for a row that sees no key (its O row is 0).
+ *
+ * Query row r is at absolute position q_offset + r and key column c at
+ * kv_offset + c; with causal != 0 key c is visible to row r iff
+ * kv_offset + c <= q_offset + r.  The offsets let a sequence-parallel caller
+ * run one block of a ring step.
+ *
+ * dtype BF16/F16: tcgen05 tensor-core kernel, head_dim 64 or 128, fp32
+ * softmax and accumulation, O in the input dtype; all strides multiples of 8
+ * elements and pointers 16-byte aligned (TMA rules).
+ * dtype F32: CUDA-core fp32 kernel, any head_dim <= 256.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *q;
+    const void *k;
+    const void *v;
+    void *o;
+    float *lse;                 /* may be NULL */
+    int64_t batch, heads, seq_q, seq_kv, head_dim;
+    int64_t q_stride[3];        /* element strides: batch, head, seq */
+    int64_t k_stride[3];
+    int64_t v_stride[3];
+    int64_t o_stride[3];
+    gae_dtype dtype;
+    int causal;
+    float scale;                /* usually 1/sqrt(head_dim) */
+    int64_t q_offset;
+    int64_t kv_offset;
+} gae_attn_args;
+
+GAE_API gae_status gae_attn_fwd(const gae_attn_args *args, void *stream);
+
+/* ------------------------------------------------------------------------
+ * INT8 attention (replaces cuda_src/waller_operator_int8.cu:27-67,
+ * waller_operator_int8_tc.cu:38-87, waller_operator_int8_tiled.cu:15-189).
+ * q, k: int8 [batch*heads, seq, head_dim] contiguous, with fp32 per-row
+ * dequantisation scales q_scale/k_scale [batch*heads, seq]; v, o: bf16
+ * [batch*heads, seq, head_dim].  logit(i,j) = int32 dot(q_i, k_j) computed
+ * exactly (tcgen05 kind::i8, int32 accumulation);
+ * score = logit * q_scale[i] * k_scale[j] * scale; softmax and P*V in fp32
+ * accumulation with P rounded to bf16.  head_dim 64 or 128.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const int8_t *q;
+    const int8_t *k;
+    const float *q_scale;
+    const float *k_scale;
+    const void *v;              /* bf16 */
+    void *o;                    /* bf16 */
+    float *lse;                 /* may be NULL */
+    int64_t batch_heads, seq, head_dim;
+    int causal;
+    float scale;
+} gae_attn_int8_args;
+
+GAE_API gae_status gae_attn_int8_fwd(const gae_attn_int8_args *args, void *stream);
+
+/* Writes the exact int32 logits L[bh][i][j] = sum_c q[bh][i][c]*k[bh][j][c]
+ * through the same tcgen05 kind::i8 tiles the attention kernel uses, for
+ * bit-exact verification (the reference's dot_int8,
+ * cuda_src/waller_operator_int8.cu:13-24).  logits: int32
+ * [batch_heads, seq_q, seq_kv]. */
+GAE_API gae_status gae_int8_logits(const int8_t *q, const int8_t *k, int64_t batch_heads,
+                           int64_t seq_q, int64_t seq_kv, int64_t head_dim,
+                           int32_t *logits, void *stream);
+
+/* Per-row symmetric int8 quantisation: scale = max|x|/127, q = rint(x/scale)
+ * clamped to +-127 (an all-zero row gets scale 0).  x: bf16 or fp32
+ * [rows, d] contiguous.  (Extension: the reference quantises on the host with
+ * a per-tensor 127 scale, cuda_src/waller_operator_int8.cu:99-100.) */
+GAE_API gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, int64_t d,
+                                  int8_t *q, float *scale, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Log-sum-exp merge of two partial attention results over disjoint key sets
+ * (the (max, sum, acc) merge of cuda_src/waller_operator_v2.cu:120-142,
+ * restated on normalised outputs): in place
+ *   m = max(lse_acc, lse_part); a = e^(lse_acc-m); b = e^(lse_part-m)
+ *   o_acc = (a*o_acc + b*o_part)/(a+b);  lse_acc = m + log(a+b).
+ * o_acc/o_part: [rows, head_dim] with row stride (elements) of dtype;
+ * lse: fp32 [rows] contiguous.  Rows with both lse = -inf are left as is.
+ * ---------------------------------------------------------------------- */
+GAE_API gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part,
+                         const float *lse_part, int64_t rows, int64_t head_dim,
+                         int64_t o_acc_row_stride, int64_t o_part_row_stride,
+                         gae_dtype dtype, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Fused pre-norm transformer layer (replaces the fused "symphony" layer,
+ * cuda_src/waller_fused_layer.cu:64-247, and the API of
+ * ate::TransformerBlock::forward, rust_src/src/transformer.rs:87-120, for a
+ * real causal attention layer at GPT-2 shape):
+ *   h   = LN1(x); qkv = h @ Wqkv + bqkv; a = causal_attention(qkv)
+ *   x1  = x + a @ Wproj + bproj
+ *   out = x1 + gelu_tanh(LN2(x1) @ Wfc + bfc) @ Wfc2 + bfc2
+ * Activations bf16 [tokens = batch*seq, d_model] contiguous; weights bf16
+ * stored [out, in] row-major (K-major for the tensor cores); biases and LN
+ * parameters fp32.  `workspace` is caller-provided device memory of at least
+ * gae_layer_workspace_bytes(...) bytes.  x and out may alias.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *ln1_gamma, *ln1_beta;   /* fp32 [d_model] */
+    const void *w_qkv, *b_qkv;          /* bf16 [3*d_model, d_model], fp32 [3*d_model] */
+    const void *w_proj, *b_proj;        /* bf16 [d_model, d_model],  fp32 [d_model] */
+    const void *ln2_gamma, *ln2_beta;   /* fp32 [d_model] */
+    const void *w_fc, *b_fc;            /* bf16 [d_ff, d_model],     fp32 [d_ff] */
+    const void *w_fc2, *b_fc2;          /* bf16 [d_model, d_ff],     fp32 [d_model] */
+} gae_layer_weights;
+
+typedef struct {
+    const void *x;              /* bf16 [batch*seq, d_model] */
+    void *out;                  /* bf16 [batch*seq, d_model] */
+    int64_t batch, seq, d_model, heads, d_ff;
+    float eps;
+    void *workspace;
+    size_t workspace_bytes;
+} gae_layer_args;
+
+GAE_API size_t gae_layer_workspace_bytes(int64_t batch, int64_t seq, int64_t d_model, int64_t d_ff);
+
+GAE_API gae_status gae_layer_fwd(const gae_layer_args *args, const gae_layer_weights *w, void *stream);
+
+/* A stack of n_layers pre-norm layers applied in order (the GPT-2 stack);
+ * ping-pongs between out and the workspace. */
+GAE_API gae_status gae_layer_stack_fwd(const gae_layer_args *args, const gae_layer_weights *w,
+                               int n_layers, void *stream);
+
+/* Row LayerNorm with the reference's semantics (population variance, eps
+ * inside the sqrt; rust_src/src/layernorm.rs:20-47): bf16 in/out, fp32
+ * gamma/beta, optional fused residual add (res may be NULL: y = LN(x);
+ * otherwise s = x + res is written to sum_out when non-NULL and y = LN(s)). */
+GAE_API gae_status gae_layernorm_fwd(const void *x, const void *res, void *sum_out, void *y,
+                             const float *gamma, const float *beta, int64_t rows,
+                             int64_t d, float eps, void *stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* GAE_H_ */

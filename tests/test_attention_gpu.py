@@ -1,0 +1,206 @@
+"""Parity of the CUDA attention kernels against the CPU oracle, through the C ABI.
+
+Tolerances (written here, as the benchmark plan states them):
+  fp32 path: max-abs error <= 1e-5 x max|ref| and relative L2 <= 1e-5 against
+             the fp32 oracle on identical inputs;
+  bf16/f16:  max-abs error <= 2e-2 against the fp32 oracle fed the same
+             bf16-rounded inputs; log-sum-exp within 1e-3 absolute.
+"""
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 2e-2
+
+
+def rel_scale(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+# ---------------------------------------------------------------- fp32 path
+@pytest.mark.parametrize("causal", [True, False])
+def test_config1_f32_host_dropin(gae, ora, causal):
+    from tests.golden.make_golden import config1_inputs, load_golden
+    q, k, v = config1_inputs()
+    out = gae.waller_operator(q, k, v, 1024, 64, 0.125, causal=causal).reshape(1024, 64)
+    ref = ora.waller_operator(q, k, v, 1024, 64, 0.125, causal=causal).reshape(1024, 64)
+    assert rel_scale(out, ref) <= 1e-5
+    assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 1e-5
+    rows, gold = load_golden("config1_causal" if causal else "config1_noncausal")
+    assert rel_scale(out[rows], gold) <= 1e-5
+
+
+def test_reference_kats_on_gpu(gae):
+    # tests/validation.rs:79-94 through the GPU drop-in
+    n, d = 4, 2
+    v = np.arange(n * d, dtype=np.float32)
+    out = gae.waller_operator(np.ones(n * d), np.ones(n * d), v, n, d, 1 / math.sqrt(d))
+    assert abs(out[0] - v[0]) <= 1e-4 and abs(out[1] - v[1]) <= 1e-4
+    # tests/validation.rs:147-163
+    n, d = 16, 8
+    i = np.arange(n * d, dtype=np.float32)
+    q = np.sin(i * np.float32(0.1)); k = np.cos(i * np.float32(0.2)); vv = np.sin(i * np.float32(0.05))
+    st = gae.standard_attention(q, k, vv, n, d, 1 / math.sqrt(d))
+    wa = gae.waller_operator_parallel(q, k, vv, n, d, 1 / math.sqrt(d))
+    assert np.abs(st - wa).max() <= 1e-4
+
+
+def test_f32_device_batched_offsets(gae, ora):
+    g = torch.Generator().manual_seed(3)
+    B, H, Nq, Nkv, D = 2, 3, 200, 330, 96
+    q = torch.randn(B, H, Nq, D, generator=g)
+    k = torch.randn(B, H, Nkv, D, generator=g)
+    v = torch.randn(B, H, Nkv, D, generator=g)
+    o, lse = gae.attention(q.cuda(), k.cuda(), v.cuda(), causal=True, q_offset=130, kv_offset=0,
+                           return_lse=True)
+    ref, rlse = ora.attention_batched(q.numpy(), k.numpy(), v.numpy(), 1 / math.sqrt(D), True,
+                                      q_offset=130, want_lse=True)
+    assert rel_scale(o.cpu().numpy(), ref) <= 1e-5
+    assert np.abs(lse.cpu().numpy() - rlse).max() <= 1e-5
+
+
+def test_f32_host_rejects_short_input(gae):
+    with pytest.raises(gae.GAEError):
+        gae.waller_operator(np.ones(7), np.ones(8), np.ones(8), 4, 2, 1.0)
+
+
+# ---------------------------------------------------------- tensor-core path
+def _rand(shape, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn(*shape, generator=g).to(dtype)
+
+
+def _check_tc(gae, ora, B, H, Nq, Nkv, D, causal, dtype=torch.bfloat16, q_offset=0,
+              kv_offset=0, layout="bhsd", seed=0):
+    q = _rand((B, H, Nq, D), dtype, seed)
+    k = _rand((B, H, Nkv, D), dtype, seed + 1)
+    v = _rand((B, H, Nkv, D), dtype, seed + 2)
+    if layout == "bshd":  # strided views of [B, N, H, D] storage
+        qd = q.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+        kd = k.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+        vd = v.transpose(1, 2).contiguous().cuda().transpose(1, 2)
+    else:
+        qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    o, lse = gae.attention(qd, kd, vd, causal=causal, q_offset=q_offset, kv_offset=kv_offset,
+                           return_lse=True)
+    torch.cuda.synchronize()
+    gae.device_status()
+    ref, rlse = ora.attention_batched(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                      1 / math.sqrt(D), causal, q_offset=q_offset,
+                                      kv_offset=kv_offset, want_lse=True)
+    got = o.float().cpu().numpy()
+    err = float(np.abs(got - ref).max())
+    assert err <= BF16_TOL, f"max-abs {err}"
+    gl = lse.cpu().numpy()
+    fin = np.isfinite(rlse)
+    assert np.array_equal(np.isfinite(gl), fin)
+    if fin.any():
+        assert np.abs(gl[fin] - rlse[fin]).max() <= 1e-3
+    return o
+
+
+@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("causal", [False, True])
+def test_tc_square(gae, ora, D, causal):
+    _check_tc(gae, ora, 1, 2, 512, 512, D, causal)
+
+
+@pytest.mark.parametrize("N", [1, 100, 128, 129, 255, 256, 257, 777])
+def test_tc_ragged_lengths(gae, ora, N):
+    _check_tc(gae, ora, 1, 2, N, N, 128, True, seed=N)
+    _check_tc(gae, ora, 1, 1, N, N, 64, False, seed=N + 7)
+
+
+def test_tc_cross_lengths(gae, ora):
+    _check_tc(gae, ora, 2, 2, 300, 1000, 128, False)
+    _check_tc(gae, ora, 1, 3, 1000, 300, 64, False)
+
+
+def test_tc_strided_bshd_layout(gae, ora):
+    _check_tc(gae, ora, 2, 4, 384, 384, 128, True, layout="bshd")
+
+
+def test_tc_fp16(gae, ora):
+    _check_tc(gae, ora, 1, 2, 384, 384, 128, True, dtype=torch.float16)
+
+
+@pytest.mark.parametrize("q_offset,kv_offset", [(512, 0), (512, 256), (0, 512), (100, 37)])
+def test_tc_ring_block_offsets(gae, ora, q_offset, kv_offset):
+    # A query block attending to one key block of a longer causal sequence.
+    _check_tc(gae, ora, 1, 2, 256, 256, 128, True, q_offset=q_offset, kv_offset=kv_offset)
+
+
+def test_tc_large_scores_rescale(gae, ora):
+    # Scores spread over a wide range exercise the lazy max rescaling.
+    B, H, N, D = 1, 1, 1024, 128
+    q = _rand((B, H, N, D), torch.float32, 9) * 4
+    k = _rand((B, H, N, D), torch.float32, 10) * 4
+    v = _rand((B, H, N, D), torch.float32, 11)
+    qb, kb, vb = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    o = gae.attention(qb.cuda(), kb.cuda(), vb.cuda(), causal=True)
+    ref = ora.attention_batched(qb.float().numpy(), kb.float().numpy(), vb.float().numpy(),
+                                1 / math.sqrt(D), True)
+    assert float(np.abs(o.float().cpu().numpy() - ref).max()) <= BF16_TOL
+
+
+def test_tc_deterministic(gae):
+    q, k, v = (_rand((2, 4, 1024, 128), torch.bfloat16, s).cuda() for s in (1, 2, 3))
+    a = gae.attention(q, k, v, causal=True)
+    b = gae.attention(q, k, v, causal=True)
+    assert torch.equal(a, b)
+
+
+def test_tc_matches_torch_sdpa(gae):
+    # Cross-check against PyTorch's own attention at a mid size.
+    q, k, v = (_rand((2, 8, 2048, 128), torch.bfloat16, s).cuda() for s in (4, 5, 6))
+    for causal in (False, True):
+        o = gae.attention(q, k, v, causal=causal)
+        r = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(),
+                                                             is_causal=causal)
+        assert float((o.float() - r).abs().max()) <= BF16_TOL
+
+
+def test_tc_rejects_bad_head_dim(gae):
+    q = torch.zeros(1, 1, 128, 96, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(gae.GAEError):
+        gae.attention(q, q, q)
+
+
+def test_tc_empty_query(gae):
+    q = torch.zeros(1, 1, 0, 128, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(1, 1, 128, 128, dtype=torch.bfloat16, device="cuda")
+    o = gae.attention(q, k, k)
+    assert o.shape == (1, 1, 0, 128)
+
+
+def test_lse_merge_matches_oracle(gae, ora):
+    g = torch.Generator().manual_seed(8)
+    rows, D = 1000, 128
+    o1 = torch.randn(rows, D, generator=g); o2 = torch.randn(rows, D, generator=g)
+    l1 = torch.randn(rows, generator=g) * 3; l2 = torch.randn(rows, generator=g) * 3
+    l2[:10] = -float("inf")
+    ro, rl = ora.lse_merge(o1.numpy(), l1.numpy(), o2.numpy(), l2.numpy())
+    a, la = o1.cuda(), l1.cuda()
+    gae.lse_merge_(a, la, o2.cuda(), l2.cuda())
+    assert rel_scale(a.cpu().numpy(), ro) <= 1e-5
+    assert np.abs(la.cpu().numpy() - rl).max() <= 1e-5
+    ab = o1.bfloat16().cuda()
+    gae.lse_merge_(ab, l1.clone().cuda(), o2.bfloat16().cuda(), l2.cuda())
+    assert float(np.abs(ab.float().cpu().numpy() - ro).max()) <= BF16_TOL
+
+
+def test_quantize_rows_int8_bit_exact(gae, ora):
+    x = _rand((64, 128), torch.float32, 12)
+    x[3] = 0
+    q, s = gae.quantize_rows_int8(x.cuda())
+    rq, rs = ora.quantize_rows_int8(x.numpy())
+    assert np.array_equal(q.cpu().numpy(), rq)
+    assert np.array_equal(s.cpu().numpy(), rs)
+    xb = x.bfloat16()
+    q, s = gae.quantize_rows_int8(xb.cuda())
+    rq, rs = ora.quantize_rows_int8(xb.float().numpy())
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
