@@ -74,40 +74,52 @@ def profile_traffic(kernel_tag):
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons.  A reader thread
+    stamps every sample with the host clock; summary() keeps the samples taken
+    inside [t0, t1], the timed region."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
+    def __init__(self, index, period_ms=50):
+        self.index, self.period_ms = index, period_ms
+        self.proc, self.samples, self.t0, self.t1 = None, [], None, None
 
-    def __enter__(self):
+    def start(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.period_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+
+        def reader():
+            for ln in self.proc.stdout:
+                self.samples.append((time.time(), ln.strip()))
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+        deadline = time.time() + 10
+        while not self.samples and time.time() < deadline:  # nvidia-smi is up
+            time.sleep(0.05)
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
+        for ts, ln in list(self.samples):
+            if self.t0 is not None and not (self.t0 <= ts <= self.t1):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -189,8 +201,8 @@ def run_reference(args, w):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="gae", choices=["gae", "reference"])
     ap.add_argument("--workload", default="mha", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -236,13 +248,16 @@ def main():
         gae.attention(q, k, v, causal=causal, out=out)
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier()
-        ev0.record(stream)
-        for _ in range(args.steps):
-            gae.attention(q, k, v, causal=causal, out=out)
-        ev1.record(stream)
-        barrier()
+    clk = ClockSampler(local).start()
+    barrier()
+    clk.t0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        gae.attention(q, k, v, causal=causal, out=out)
+    ev1.record(stream)
+    barrier()
+    clk.t1 = time.time()
+    clk.stop()
     gae.device_status()
     t_ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = t_ms / args.steps

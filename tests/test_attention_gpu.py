@@ -188,9 +188,11 @@ def test_lse_merge_matches_oracle(gae, ora):
     gae.lse_merge_(a, la, o2.cuda(), l2.cuda())
     assert rel_scale(a.cpu().numpy(), ro) <= 1e-5
     assert np.abs(la.cpu().numpy() - rl).max() <= 1e-5
-    ab = o1.bfloat16().cuda()
-    gae.lse_merge_(ab, l1.clone().cuda(), o2.bfloat16().cuda(), l2.cuda())
-    assert float(np.abs(ab.float().cpu().numpy() - ro).max()) <= BF16_TOL
+    b1, b2 = o1.bfloat16(), o2.bfloat16()
+    rbo, _ = ora.lse_merge(b1.float().numpy(), l1.numpy(), b2.float().numpy(), l2.numpy())
+    ab = b1.cuda()
+    gae.lse_merge_(ab, l1.clone().cuda(), b2.cuda(), l2.cuda())
+    assert float(np.abs(ab.float().cpu().numpy() - rbo).max()) <= BF16_TOL
 
 
 def test_quantize_rows_int8_bit_exact(gae, ora):
