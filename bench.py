@@ -141,44 +141,51 @@ def make_inputs(torch, w, device, seed):
     return [torch.randn(*shape, generator=g).to(torch.bfloat16).to(device) for _ in range(3)]
 
 
-def cpu_sample(w, threads_note=True):
-    """Times the oracle's Waller recurrence on one (batch, head) slice of the
-    workload (all query rows, their full causal key range).  Returns
-    (TFLOPS, seconds, description)."""
+def cpu_sample(w, slices=8, rows_cap=None):
+    """Times the oracle's Waller recurrence (OpenMP over rows, all host
+    threads) on `slices` (batch, head) slices of the workload: every query row
+    with its full (causal) key range, or `rows_cap` evenly spaced rows per
+    slice.  Returns (TFLOPS, seconds, description, threads)."""
     import numpy as np
     from oracle import oracle
     N, D = w["N"], w["D"]
     rng = np.random.default_rng(1234)
-    q, k, v = (rng.standard_normal((1, 1, N, D)).astype(np.float32) for _ in range(3))
-    rows = None
-    n_rows = N
-    if N > 16384:  # long workload: evenly spaced rows, full key range each
-        n_rows = 2048
-        rows = np.linspace(0, N - 1, n_rows).round().astype(np.int64)
+    q, k, v = (rng.standard_normal((1, slices, N, D)).astype(np.float32) for _ in range(3))
+    n_rows = N if rows_cap is None else min(N, rows_cap)
+    rows = None if n_rows == N else np.linspace(0, N - 1, n_rows).round().astype(np.int64)
     oracle.lib()
     t0 = time.perf_counter()
     oracle.attention_batched(q, k, v, 1.0 / math.sqrt(D), w["causal"], rows=rows)
     dt = time.perf_counter() - t0
     if rows is None:
-        flops = attn_flops(1, 1, N, N, D, w["causal"])
-        desc = f"one (batch, head) slice: {N} query rows x full {'causal ' if w['causal'] else ''}key range"
+        flops = attn_flops(1, slices, N, N, D, w["causal"])
+        desc = (f"{slices} (batch, head) slice(s) of {N} query rows, each with its full "
+                f"{'causal ' if w['causal'] else ''}key range")
     else:
         pairs = float(np.sum(rows + 1)) if w["causal"] else float(n_rows * N)
-        flops = 4.0 * D * pairs
-        desc = f"{n_rows} evenly spaced query rows of one head, full causal key range each"
+        flops = 4.0 * D * pairs * slices
+        desc = (f"{slices} slice(s) x {n_rows} evenly spaced query rows, each with its full "
+                f"{'causal ' if w['causal'] else ''}key range")
     return flops / dt / 1e12, dt, desc, oracle.num_threads()
 
 
 def run_reference(args, w):
+    """The reference arm: the CPU path on a bounded sample per step, sized so
+    that warm-up plus timed steps take about two minutes in total."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    # Calibrate: seconds per row of one slice (full key range).
+    _, s_cal, _, _ = cpu_sample(w, slices=1, rows_cap=256)
+    per_row = s_cal / 256
+    budget = 120.0 / (args.steps + args.warmup)
+    rows_cap = int(max(64, min(w["N"], budget / per_row)))
     for _ in range(args.warmup):
-        cpu_sample(w)
+        cpu_sample(w, slices=1, rows_cap=rows_cap)
     vals, secs = [], []
     desc, threads = "", 1
     for _ in range(args.steps):
-        v, s, desc, threads = cpu_sample(w)
+        v, s, desc, threads = cpu_sample(w, slices=1, rows_cap=rows_cap)
         vals.append(v)
         secs.append(s)
     value = statistics.mean(vals)
@@ -190,7 +197,7 @@ def run_reference(args, w):
         "config": {"workload": w["cfg"], "B": w["B"], "H": w["H"], "seq_len": w["N"],
                    "head_dim": w["D"], "causal": w["causal"]},
         "cpu_baseline": {"value": value, "unit": "TFLOPS", "cores": threads, "kind": "port",
-                         "sample": desc},
+                         "sample": desc + " per step"},
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -304,7 +311,7 @@ def main():
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v_cpu, s_cpu, desc, threads = cpu_sample(w)
+        v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=None if w["N"] <= 16384 else 2048)
         cpu = {"value": v_cpu, "unit": "TFLOPS", "cores": threads, "kind": "port",
                "sample": desc + f" ({s_cpu:.1f} s)"}
 

@@ -9,11 +9,15 @@
 // 429 (Hopper TMA + wgmma); this kernel is a new design for tcgen05/TMEM.
 //
 // CTA = 256 query rows of one (batch, head): two 128-row Q tiles that
-// ping-pong on the tensor core.  Warp roles (320 threads):
+// ping-pong on the tensor core.  Warp roles (384 threads, 3 warpgroups):
 //   warps 0-3  softmax group 0  (Q tile 0, TMEM lanes 0..127, thread = row)
 //   warps 4-7  softmax group 1  (Q tile 1)
 //   warp  8    TMA producer     (Q once, then K_j, V_j into a smem ring)
 //   warp  9    MMA issuer       (owns the TMEM allocation)
+//   warps 10-11 idle
+// Registers: launched at 168 per thread; the producer warpgroup shrinks to
+// 72 and the two softmax warpgroups grow to 216 (2*128*216 + 128*72 =
+// 384*168, so the re-balancing always fits).
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 after it.
 // P_i (bf16, 2 per column) overwrites the first 64 columns of S_i and feeds
 // the P*V MMA straight from TMEM.  Per K/V tile j the MMA warp issues
@@ -35,9 +39,11 @@
 namespace gae {
 
 struct AttnParams {
-    CUtensorMap tm_q;  // dims {D, Nq, H, B}, box {64, 128, 1, 1}, 128B swizzle
+    CUtensorMap tm_q;  // dims {D, Nq, H, B}, box {128 bytes, 128, 1, 1}, 128B swizzle
     CUtensorMap tm_k;  // dims {D, Nkv, H, B}
     CUtensorMap tm_v;
+    CUtensorMap tm_ks;      // int8 mode: k_scale as dims {Nkv, B*H}, box {128, 1}
+    const float *q_scale;   // int8 mode: [B*H, Nq]
     void *o;
     float *lse;
     int64_t o_sb, o_sh, o_ss;  // element strides of O
@@ -58,28 +64,43 @@ enum AttnWaitSite : unsigned {
     kSiteDone = 0x107,
 };
 
-template <int D>
+enum AttnMode : int { kModeBF16 = 0, kModeF16 = 1, kModeInt8 = 2 };
+
+template <int D, int kMode>
 struct AttnCfg {
-    static constexpr int kBlockM = 128;                  // rows per Q tile
-    static constexpr int kBlockN = 128;                  // keys per K/V tile
-    static constexpr int kHalves = D / 64;               // 128-byte swizzle boxes per row
-    static constexpr int kBoxBytes = 128 * 128;          // 128 rows x 128 B
-    static constexpr int kTileBytes = kHalves * kBoxBytes;
-    static constexpr int kStages = (D == 128) ? 4 : 8;   // K/V ring slots
-    static constexpr int kQBytes = 2 * kTileBytes;
-    static constexpr int kRingBytes = kStages * kTileBytes;
+    static constexpr bool kInt8 = kMode == kModeInt8;
+    static constexpr int kBlockM = 128;                      // rows per Q tile
+    static constexpr int kBlockN = 128;                      // keys per K/V tile
+    static constexpr int kBoxBytes = 128 * 128;              // 128 rows x 128 B
+    static constexpr int kQKRowBytes = D * (kInt8 ? 1 : 2);  // Q/K row
+    static constexpr int kQKBoxes = kQKRowBytes / 128;       // 128-byte swizzle boxes per Q/K row
+    static constexpr int kVBoxes = D * 2 / 128;              // V is 16-bit in every mode
+    static constexpr int kQTileBytes = kQKBoxes * kBoxBytes;
+    static constexpr int kKTileBytes = kQKBoxes * kBoxBytes;
+    static constexpr int kVTileBytes = kVBoxes * kBoxBytes;
+    static constexpr int kKScaleBytes = kInt8 ? kBlockN * 4 : 0;  // per-key scales after K
+    static constexpr int kSlotBytes = kVTileBytes;               // >= K tile + its scales
+    static constexpr int kStages = (D == 128) ? (kInt8 ? 5 : 4) : 8;  // K/V ring slots
+    static constexpr int kQBytes = 2 * kQTileBytes;
+    static constexpr int kRingBytes = kStages * kSlotBytes;
     static constexpr int kBarOffset = kQBytes + kRingBytes;
     // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done
     static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
-    static constexpr int kThreads = 320;
+    static constexpr int kThreads = 384;
+    static constexpr int kRegsSoftmax = 216, kRegsProducer = 72;
+    static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer <= kThreads * 168, "register split");
+    static_assert(kInt8 ? (D == 128) : (D == 64 || D == 128), "unsupported head_dim");
+    static_assert(kKTileBytes + kKScaleBytes <= kSlotBytes, "K slot too small");
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
-template <int D, bool kBF16>
-__global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
-    using Cfg = AttnCfg<D>;
+template <int D, int kMode>
+__global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
+    using Cfg = AttnCfg<D, kMode>;
+    constexpr bool kBF16 = kMode != kModeF16;  // P and O are bf16 in bf16 and int8 modes
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128B-swizzle atoms.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -141,17 +162,21 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
     tc_fence_after();
     const uint32_t tmem = (n_kv > 0) ? *tmem_base_slot : 0u;
 
-    if (warp == 8) {
+    if (warp >= 10) {
+        regs_dec<Cfg::kRegsProducer>();
+    } else if (warp == 8) {
         // ------------------------------------------------------ TMA producer
+        regs_dec<Cfg::kRegsProducer>();
         if (lane == 0 && n_kv > 0) {
             tma_prefetch_desc(&p.tm_q);
             tma_prefetch_desc(&p.tm_k);
             tma_prefetch_desc(&p.tm_v);
+            if (Cfg::kInt8) tma_prefetch_desc(&p.tm_ks);
             mbar_expect_tx(bar_q(), Cfg::kQBytes);
             for (int t = 0; t < 2; ++t)
-                for (int hf = 0; hf < Cfg::kHalves; ++hf)
-                    tma_load_4d(sQ + t * Cfg::kTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
-                                hf * 64, q0 + t * 128, h, b);
+                for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
+                    tma_load_4d(sQ + t * Cfg::kQTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
+                                hf * 128 / (Cfg::kInt8 ? 1 : 2), q0 + t * 128, h, b);
             bool ok = true;
             int issued = 0;
             for (int j = 0; j < n_kv && ok; ++j) {
@@ -161,12 +186,21 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
                     const int use = item / Cfg::kStages;
                     if (use > 0) ok = mbar_wait(bar_kv_empty(slot), (use - 1) & 1, kSiteKvEmpty, abort_flag);
                     if (!ok) break;
-                    const uint32_t dst = sRing + slot * Cfg::kTileBytes;
-                    const CUtensorMap *m = kv ? &p.tm_v : &p.tm_k;
-                    mbar_expect_tx(bar_kv_full(slot), Cfg::kTileBytes);
-                    for (int hf = 0; hf < Cfg::kHalves; ++hf)
-                        tma_load_4d(dst + hf * Cfg::kBoxBytes, m, bar_kv_full(slot), hf * 64,
-                                    j * Cfg::kBlockN, h, b);
+                    const uint32_t dst = sRing + slot * Cfg::kSlotBytes;
+                    if (kv) {
+                        mbar_expect_tx(bar_kv_full(slot), Cfg::kVTileBytes);
+                        for (int hf = 0; hf < Cfg::kVBoxes; ++hf)
+                            tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_v, bar_kv_full(slot),
+                                        hf * 64, j * Cfg::kBlockN, h, b);
+                    } else {
+                        mbar_expect_tx(bar_kv_full(slot), Cfg::kKTileBytes + Cfg::kKScaleBytes);
+                        for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
+                            tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_k, bar_kv_full(slot),
+                                        hf * 128 / (Cfg::kInt8 ? 1 : 2), j * Cfg::kBlockN, h, b);
+                        if (Cfg::kInt8)
+                            tma_load_2d(dst + Cfg::kKTileBytes, &p.tm_ks, bar_kv_full(slot),
+                                        j * Cfg::kBlockN, bh);
+                    }
                     issued = item + 1;
                 }
             }
@@ -179,25 +213,32 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
         }
     } else if (warp == 9) {
         // ---------------------------------------------------------- MMA issuer
+        regs_dec<Cfg::kRegsProducer>();
         if (lane == 0 && n_kv > 0) {
-            constexpr uint32_t idesc_qk = idesc_f16(128, 128, kBF16, false, false);
+            constexpr uint32_t idesc_qk =
+                Cfg::kInt8 ? idesc_i8(128, 128) : idesc_f16(128, 128, kBF16, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, false, true);
             bool ok = mbar_wait(bar_q(), 0, kSiteQ, abort_flag);
             auto issue_qk = [&](int i, int slot) {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
-                const uint32_t qa = sQ + i * Cfg::kTileBytes;
-                const uint32_t kb = sRing + slot * Cfg::kTileBytes;
+                const uint32_t qa = sQ + i * Cfg::kQTileBytes;
+                const uint32_t kb = sRing + slot * Cfg::kSlotBytes;
+                // One MMA consumes 32 bytes of K (16 bf16 or 32 int8 elements).
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
+                for (int kk = 0; kk < Cfg::kQKRowBytes / 32; ++kk) {
                     const uint32_t off = (kk >> 2) * Cfg::kBoxBytes + (kk & 3) * 32;
-                    umma_f16_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024),
-                                smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+                    if constexpr (Cfg::kInt8)
+                        umma_i8_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024),
+                                   smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
+                    else
+                        umma_f16_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024),
+                                    smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
                 }
             };
             auto issue_pv = [&](int i, int slot, bool acc) {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColO1 : Cfg::kColO0);
                 const uint32_t p_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
-                const uint32_t vb = sRing + slot * Cfg::kTileBytes;
+                const uint32_t vb = sRing + slot * Cfg::kSlotBytes;
 #pragma unroll
                 for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk) {
                     umma_f16_ts(d_tmem, p_tmem + kk * 8,
@@ -225,10 +266,12 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
                     tc_fence_after();
                     issue_pv(1, v_slot, j - 1 > 0);
                     umma_commit(bar_kv_empty(v_slot));
+                    // int8: both softmax groups have read K_{j-1}'s scales from its slot.
+                    if (Cfg::kInt8) mbar_arrive(bar_kv_empty(((2 * j - 2) % Cfg::kStages)));
                 }
                 issue_qk(1, k_slot);
                 umma_commit(bar_s(1));
-                umma_commit(bar_kv_empty(k_slot));
+                if (!Cfg::kInt8) umma_commit(bar_kv_empty(k_slot));
             }
             if (ok) {
                 const int v_item = 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
@@ -245,6 +288,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
                     issue_pv(1, v_slot, n_kv > 1);
                     umma_commit(bar_o(1));
                     umma_commit(bar_kv_empty(v_slot));
+                    if (Cfg::kInt8) mbar_arrive(bar_kv_empty((2 * n_kv - 2) % Cfg::kStages));
                 }
             }
             // Drain: every MMA this thread issued has completed before TMEM is
@@ -254,6 +298,7 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
         }
     } else {
         // ------------------------------------------------------ softmax groups
+        regs_inc<Cfg::kRegsSoftmax>();
         const int grp = warp >> 2;       // Q tile 0 or 1
         const int wq = warp & 3;         // TMEM lane quarter
         const int row = wq * 32 + lane;  // row within the Q tile
@@ -262,7 +307,15 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
         const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
         const uint32_t tS = tmem + lane_off + (grp ? Cfg::kColS1 : Cfg::kColS0);
         const uint32_t tO = tmem + lane_off + (grp ? Cfg::kColO1 : Cfg::kColO0);
-        const float sl2 = p.scale_log2;
+        // Factor that takes a raw score to the log2 domain: scale*log2(e), times
+        // the query row's dequantisation scale in int8 mode.
+        float sl2 = p.scale_log2;
+        if constexpr (Cfg::kInt8)
+            sl2 *= (q_local < p.Nq) ? p.q_scale[(int64_t)bh * p.Nq + q_local] : 0.f;
+        // A zero factor (zero scale, or an all-zero int8 query row) makes every
+        // visible score equal; a tiny positive factor keeps that result while
+        // masked (-inf) entries still map to probability 0 instead of NaN.
+        sl2 = fmaxf(sl2, 1e-30f);
 
         float m_run = -INFINITY;  // exponent base, log2 domain (scaled)
         float l_run = 0.f;
@@ -279,12 +332,39 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
                 tmem_ld32(tS + 64, r2);
                 tmem_ld32(tS + 96, r3);
                 tmem_wait_ld();
+                if constexpr (Cfg::kInt8) {
+                    // Exact int32 logits times the keys' dequantisation scales.  The
+                    // scales arrived with K_j; its slot is released only after both
+                    // softmax groups finished tile j.
+                    const int slot = (2 * j) % Cfg::kStages;
+                    if (!mbar_wait(bar_kv_full(slot), ((2 * j) / Cfg::kStages) & 1, kSiteKvFull,
+                                   abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const float4 *ks = reinterpret_cast<const float4 *>(
+                        smem + Cfg::kQBytes + slot * Cfg::kSlotBytes + Cfg::kKTileBytes);
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    s[e] = __uint_as_float(r0[e]);
-                    s[32 + e] = __uint_as_float(r1[e]);
-                    s[64 + e] = __uint_as_float(r2[e]);
-                    s[96 + e] = __uint_as_float(r3[e]);
+                    for (int e4 = 0; e4 < 8; ++e4) {
+                        const float4 a = ks[e4], bq = ks[8 + e4], c = ks[16 + e4], d = ks[24 + e4];
+                        const float ka[4] = {a.x, a.y, a.z, a.w}, kb4[4] = {bq.x, bq.y, bq.z, bq.w};
+                        const float kc[4] = {c.x, c.y, c.z, c.w}, kd[4] = {d.x, d.y, d.z, d.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            s[4 * e4 + u] = (float)(int)r0[4 * e4 + u] * ka[u];
+                            s[32 + 4 * e4 + u] = (float)(int)r1[4 * e4 + u] * kb4[u];
+                            s[64 + 4 * e4 + u] = (float)(int)r2[4 * e4 + u] * kc[u];
+                            s[96 + 4 * e4 + u] = (float)(int)r3[4 * e4 + u] * kd[u];
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        s[e] = __uint_as_float(r0[e]);
+                        s[32 + e] = __uint_as_float(r1[e]);
+                        s[64 + e] = __uint_as_float(r2[e]);
+                        s[96 + e] = __uint_as_float(r3[e]);
+                    }
                 }
             }
             // Masking: causal boundary and the ragged end of the key range.
@@ -298,28 +378,47 @@ __global__ void __launch_bounds__(320, 1) attn_fwd_sm100_kernel(const __grid_con
 #pragma unroll
                 for (int c = 0; c < 128; ++c) s[c] = (c < limit) ? s[c] : -INFINITY;
             }
-            float mx = s[0];
+            // Row max: four independent chains of three-input max.
+            float mq[4];
 #pragma unroll
-            for (int c = 1; c < 128; ++c) mx = fmaxf(mx, s[c]);
-            const float m_tile = mx * sl2;
+            for (int k4 = 0; k4 < 4; ++k4) {
+                float m = s[32 * k4];
+#pragma unroll
+                for (int i = 1; i < 31; i += 2) m = fmax3(m, s[32 * k4 + i], s[32 * k4 + i + 1]);
+                mq[k4] = fmaxf(m, s[32 * k4 + 31]);
+            }
+            const float mx = fmax3(fmaxf(mq[0], mq[1]), mq[2], mq[3]);
+            const float m_tile = (mx == -INFINITY) ? -INFINITY : mx * sl2;
             float alpha = 1.f;
             if (m_tile > m_run + 8.f) {  // also true while m_run == -inf and the tile sees a key
                 alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_tile);
                 m_run = m_tile;
             }
             const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            float rs = 0.f;
+            // p = 2^(s*sl2 - m): packed fp32x2 FMA, MUFU ex2, packed partial sums
+            // (four independent pair accumulators).
+            const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_use, -m_use);
+            uint64_t acc2[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const float p0 = ex2_approx(fmaf(s[c * 32 + 2 * e], sl2, -m_use));
-                    const float p1 = ex2_approx(fmaf(s[c * 32 + 2 * e + 1], sl2, -m_use));
-                    rs += p0 + p1;
+                    const uint64_t x = f2_fma(f2_pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), sl2x2, negm2);
+                    float x0, x1;
+                    f2_unpack(x, x0, x1);
+                    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+                    acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
                     pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }
                 tmem_st16(tS + c * 16, pk);
+            }
+            float rs;
+            {
+                float a0, a1, b0, b1;
+                f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), a0, a1);
+                (void)b0; (void)b1;
+                rs = a0 + a1;
             }
             l_run = l_run * alpha + rs;
             // Rescale O_i when the base moved (warp-uniform: tcgen05.ld/st are

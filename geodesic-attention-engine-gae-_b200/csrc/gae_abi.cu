@@ -89,6 +89,35 @@ gae_status set_smem(Kern k, int bytes) {
     return GAE_OK;
 }
 
+// 2-D fp32 map over a [rows, n] row-major array, box {128, 1}, no swizzle
+// (the per-key int8 dequantisation scales).
+gae_status make_map_2d_f32(CUtensorMap *m, const void *ptr, int64_t n, int64_t rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    if ((n * 4) % 16 != 0)
+        return fail(GAE_ERR_INVALID_ARG, "int8 attention needs seq %% 4 == 0 (16-byte scale rows)");
+    cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(n * 4)};
+    cuuint32_t box[2] = {128, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(ptr), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GAE_OK;
+}
+
+template <int D, int kMode>
+gae_status launch_tc(const gae::AttnParams &p, dim3 grid, cudaStream_t st) {
+    auto kern = gae::attn_fwd_sm100_kernel<D, kMode>;
+    constexpr int smem = gae::AttnCfg<D, kMode>::kSmemBytes;
+    gae_status s = set_smem(kern, smem);
+    if (s != GAE_OK) return s;
+    kern<<<grid, gae::AttnCfg<D, kMode>::kThreads, smem, st>>>(p);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
 // ------------------------------------------------------------ attention
 gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     const bool bf16 = a->dtype == GAE_DTYPE_BF16;
@@ -108,6 +137,8 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     if (a->batch * a->heads > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch*heads > 65535");
     if (a->seq_q > (1ll << 30) || a->seq_kv > (1ll << 30))
         return fail(GAE_ERR_UNSUPPORTED, "sequence longer than 2^30");
+    if (!(a->scale >= 0.f))
+        return fail(GAE_ERR_UNSUPPORTED, "tensor-core attention needs a non-negative scale");
 
     gae::AttnParams p;
     memset(&p, 0, sizeof(p));
@@ -138,19 +169,64 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     p.kv_offset = a->kv_offset;
     dim3 grid(p.n_qpairs, (unsigned)(a->batch * a->heads));
 
-#define GAE_LAUNCH_TC(DD, BF)                                                              \
-    do {                                                                                   \
-        auto kern = gae::attn_fwd_sm100_kernel<DD, BF>;                                    \
-        constexpr int smem = gae::AttnCfg<DD>::kSmemBytes;                                 \
-        if ((s = set_smem(kern, smem)) != GAE_OK) return s;                                \
-        kern<<<grid, gae::AttnCfg<DD>::kThreads, smem, st>>>(p);                           \
-    } while (0)
     if (D == 128) {
-        if (bf16) GAE_LAUNCH_TC(128, true); else GAE_LAUNCH_TC(128, false);
+        if (bf16) s = launch_tc<128, gae::kModeBF16>(p, grid, st);
+        else s = launch_tc<128, gae::kModeF16>(p, grid, st);
     } else {
-        if (bf16) GAE_LAUNCH_TC(64, true); else GAE_LAUNCH_TC(64, false);
+        if (bf16) s = launch_tc<64, gae::kModeBF16>(p, grid, st);
+        else s = launch_tc<64, gae::kModeF16>(p, grid, st);
     }
-#undef GAE_LAUNCH_TC
+    return s;
+}
+
+gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st) {
+    const int64_t D = a->head_dim, BH = a->batch_heads, N = a->seq;
+    if (D != 128) return fail(GAE_ERR_UNSUPPORTED, "int8 attention supports head_dim 128, got %lld", (long long)D);
+    if (BH > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch_heads > 65535");
+    if (N > (1ll << 30)) return fail(GAE_ERR_UNSUPPORTED, "sequence longer than 2^30");
+    const void *ptrs[6] = {a->q, a->k, a->q_scale, a->k_scale, a->v, a->o};
+    for (const void *pp : ptrs)
+        if (!pp) return fail(GAE_ERR_INVALID_ARG, "NULL pointer in int8 attention arguments");
+        else if (!aligned16(pp)) return fail(GAE_ERR_INVALID_ARG, "int8 attention pointers must be 16-byte aligned");
+    if (!(a->scale >= 0.f)) return fail(GAE_ERR_UNSUPPORTED, "negative or NaN scale");
+    gae::AttnParams p;
+    memset(&p, 0, sizeof(p));
+    gae_status s;
+    // [BH, N, D] viewed as batch = BH, heads = 1.
+    if ((s = make_map_4d(&p.tm_q, a->q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, BH, 1, N, D, N * D, N * D, D, 128)) != GAE_OK) return s;
+    if ((s = make_map_4d(&p.tm_k, a->k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, BH, 1, N, D, N * D, N * D, D, 128)) != GAE_OK) return s;
+    if ((s = make_map_4d(&p.tm_v, a->v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, BH, 1, N, D, N * D, N * D, D, 128)) != GAE_OK) return s;
+    if ((s = make_map_2d_f32(&p.tm_ks, a->k_scale, N, BH)) != GAE_OK) return s;
+    p.q_scale = a->q_scale;
+    p.o = a->o;
+    p.lse = a->lse;
+    p.o_sb = N * D; p.o_sh = N * D; p.o_ss = D;
+    p.B = (int)BH; p.H = 1; p.Nq = (int)N; p.Nkv = (int)N;
+    p.n_qpairs = (int)((N + 255) / 256);
+    p.causal = a->causal ? 1 : 0;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    dim3 grid(p.n_qpairs, (unsigned)BH);
+    return launch_tc<128, gae::kModeInt8>(p, grid, st);
+}
+
+gae_status launch_int8_logits(const int8_t *q, const int8_t *k, int64_t BH, int64_t Nq, int64_t Nkv,
+                              int64_t D, int32_t *out, cudaStream_t st) {
+    if (D != 128) return fail(GAE_ERR_UNSUPPORTED, "int8 logits support head_dim 128");
+    if (!q || !k || !out) return fail(GAE_ERR_INVALID_ARG, "NULL pointer");
+    if (!aligned16(q) || !aligned16(k)) return fail(GAE_ERR_INVALID_ARG, "q/k must be 16-byte aligned");
+    if (BH > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch_heads > 65535");
+    gae::Int8LogitsParams p;
+    memset(&p, 0, sizeof(p));
+    gae_status s;
+    if ((s = make_map_4d(&p.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, BH, 1, Nq, D, Nq * D, Nq * D, D, 128)) != GAE_OK) return s;
+    if ((s = make_map_4d(&p.tm_k, k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, BH, 1, Nkv, D, Nkv * D, Nkv * D, D, 128)) != GAE_OK) return s;
+    p.out = out;
+    p.Nq = (int)Nq;
+    p.Nkv = (int)Nkv;
+    constexpr int smem = 32768 + 64 + 1024;
+    if ((s = set_smem(gae::int8_logits_kernel, smem)) != GAE_OK) return s;
+    dim3 grid((unsigned)((Nq + 127) / 128), (unsigned)((Nkv + 127) / 128), (unsigned)BH);
+    gae::int8_logits_kernel<<<grid, 128, smem, st>>>(p);
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }
@@ -359,6 +435,23 @@ gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part, const 
     return GAE_OK;
 }
 
+gae_status gae_attn_int8_fwd(const gae_attn_int8_args *a, void *stream) {
+    if (!a) return fail(GAE_ERR_INVALID_ARG, "args is NULL");
+    if (a->batch_heads < 1 || a->seq < 0 || a->head_dim < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid int8 attention shape");
+    if (a->seq == 0) return GAE_OK;
+    return launch_attn_int8(a, static_cast<cudaStream_t>(stream));
+}
+
+gae_status gae_int8_logits(const int8_t *q, const int8_t *k, int64_t batch_heads, int64_t seq_q,
+                           int64_t seq_kv, int64_t head_dim, int32_t *logits, void *stream) {
+    if (batch_heads < 1 || seq_q < 0 || seq_kv < 0 || head_dim < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid int8 logits shape");
+    if (seq_q == 0 || seq_kv == 0) return GAE_OK;
+    return launch_int8_logits(q, k, batch_heads, seq_q, seq_kv, head_dim, logits,
+                              static_cast<cudaStream_t>(stream));
+}
+
 gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, int64_t d,
                                   int8_t *q, float *scale, void *stream) {
     if (rows == 0) return GAE_OK;
@@ -384,13 +477,6 @@ gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, 
 // Entry points whose kernels are not in this build yet: they validate nothing
 // and report GAE_ERR_UNSUPPORTED so that a caller fails loudly.
 extern "C" {
-gae_status gae_attn_int8_fwd(const gae_attn_int8_args *, void *) {
-    return fail(GAE_ERR_UNSUPPORTED, "gae_attn_int8_fwd: not built");
-}
-gae_status gae_int8_logits(const int8_t *, const int8_t *, int64_t, int64_t, int64_t, int64_t,
-                           int32_t *, void *) {
-    return fail(GAE_ERR_UNSUPPORTED, "gae_int8_logits: not built");
-}
 size_t gae_layer_workspace_bytes(int64_t, int64_t, int64_t, int64_t) { return 0; }
 gae_status gae_layer_fwd(const gae_layer_args *, const gae_layer_weights *, void *) {
     return fail(GAE_ERR_UNSUPPORTED, "gae_layer_fwd: not built");
