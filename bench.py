@@ -7,6 +7,9 @@ Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
   mha            BASELINE config 2, causal: B=4, H=16, N=8192, head_dim=128 (default)
   mha-noncausal  the same, non-causal
   long           config 5, causal: one sequence, H=8, head_dim=128, N=131072
+  ring           config 5, causal: one sequence of N=1,048,576 (H=8, head_dim=128)
+                 sharded over the N GPUs (contiguous N/P shards, ring attention with
+                 zig-zag balance, K/V rotated by NCCL send/recv; strong scaling)
 One step = one fused attention forward over the whole batch.  FLOPs count only
 visible (unmasked) score entries: 4*d per (query, key) pair, causal pairs
 N(N+1)/2 per head.  Inputs (3 x 128 MiB for mha) exceed the 126 MB L2, so no
@@ -14,7 +17,7 @@ flush between steps is needed.
 
 --gpus N > 1 (torchrun, one process per GPU): every rank runs its own batch of
 the workload (weak scaling; attention over independent (batch, head) units
-needs no exchange).  Timing: CUDA events on the launching stream, barrier +
+needs no exchange), except for `ring`, where the ranks share one sequence.  Timing: CUDA events on the launching stream, barrier +
 synchronize on both sides, max over ranks.
 
 --impl reference: the reference's CPU attention path (the oracle's restatement
@@ -41,6 +44,7 @@ WORKLOADS = {
     "mha": dict(B=4, H=16, N=8192, D=128, causal=True, cfg="config2-causal"),
     "mha-noncausal": dict(B=4, H=16, N=8192, D=128, causal=False, cfg="config2-noncausal"),
     "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
+    "ring": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M", ring=True),
 }
 METRIC = "fused-attention TFLOPS (bf16 d=128)"
 
@@ -245,14 +249,29 @@ def main():
         return float(t.item())
 
     B, H, N, D, causal = w["B"], w["H"], w["N"], w["D"], w["causal"]
-    q, k, v = make_inputs(torch, w, dev, 1000 + rank)
-    out = torch.empty_like(q)
+    is_ring = bool(w.get("ring"))
     stream = torch.cuda.current_stream()
-    flops = attn_flops(B, H, N, N, D, causal)
+    if is_ring:
+        from gae_b200 import ring
+        S = N // world
+        ws = dict(w, N=S)
+        q, k, v = make_inputs(torch, ws, dev, 1000 + rank)
+        out = torch.empty_like(q)
+        flops = attn_flops(B, H, N, N, D, causal) / world  # per rank share of the job
+
+        def run_step(q, k, v):
+            out.copy_(ring.ring_attention(q, k, v, causal=causal))
+    else:
+        q, k, v = make_inputs(torch, w, dev, 1000 + rank)
+        out = torch.empty_like(q)
+        flops = attn_flops(B, H, N, N, D, causal)
+
+        def run_step(q, k, v):
+            gae.attention(q, k, v, causal=causal, out=out)
 
     # ---- device-resident timing (value, roofline) -------------------------
     for _ in range(args.warmup):
-        gae.attention(q, k, v, causal=causal, out=out)
+        run_step(q, k, v)
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(local).start()
@@ -260,7 +279,7 @@ def main():
     clk.t0 = time.time()
     ev0.record(stream)
     for _ in range(args.steps):
-        gae.attention(q, k, v, causal=causal, out=out)
+        run_step(q, k, v)
     ev1.record(stream)
     barrier()
     clk.t1 = time.time()
@@ -269,6 +288,10 @@ def main():
     t_ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = t_ms / args.steps
     value = world * flops / (ms_step * 1e-3) / 1e12
+
+    # kernels of this library per step: the ring runs 3 block pairs + 1 merge at
+    # P=1 and 2 pairs + 2 merges per further step (zig-zag balance).
+    launches_per_step = 4 + 4 * (world - 1)
 
     # ---- end to end through the public API with host buffers ---------------
     hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
@@ -279,7 +302,7 @@ def main():
         dq.copy_(hq, non_blocking=True)
         dk.copy_(hk, non_blocking=True)
         dv.copy_(hv, non_blocking=True)
-        gae.attention(dq, dk, dv, causal=causal, out=out)
+        run_step(dq, dk, dv)
         hout.copy_(out, non_blocking=True)
 
     for _ in range(2):
@@ -318,15 +341,16 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "strong" if is_ring else "weak",
+        "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": w["cfg"], "B": B, "H": H, "seq_len": N, "head_dim": D,
-                   "causal": causal, "global_batch": B * world,
-                   "parallelism": f"dp{world}" if world > 1 else "single",
+                   "causal": causal, "global_batch": B if is_ring else B * world,
+                   "parallelism": (f"ring-sp{world}" if is_ring else f"dp{world}") if world > 1 else "single",
                    "l2": "inputs larger than L2 (no flush)"},
         "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,
                 "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (launches_per_step if is_ring else 1),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),

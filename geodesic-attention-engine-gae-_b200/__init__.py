@@ -93,7 +93,7 @@ def lib():
     L.gae_attn_int8_fwd.argtypes = [C.POINTER(AttnInt8Args), vp]
     L.gae_int8_logits.argtypes = [vp, vp, i64, i64, i64, i64, vp, vp]
     L.gae_quantize_rows_int8.argtypes = [vp, C.c_int, i64, i64, vp, vp, vp]
-    L.gae_lse_merge.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, C.c_int, vp]
+    L.gae_lse_merge.argtypes = [vp, vp, vp, vp, i64, i64, i64, i64, C.c_int, C.c_int, vp]
     L.gae_layer_workspace_bytes.restype = sz
     L.gae_layer_workspace_bytes.argtypes = [i64, i64, i64, i64]
     L.gae_layer_fwd.argtypes = [vp, vp, vp]
@@ -190,16 +190,20 @@ def attention(q, k, v, *, causal: bool = False, scale: float | None = None, q_of
 
 
 def lse_merge_(o_acc, lse_acc, o_part, lse_part, stream=None):
-    """In-place log-sum-exp merge of a partial result into an accumulator."""
+    """In-place log-sum-exp merge of a partial result into an accumulator.
+
+    o_acc/o_part: contiguous [..., D] (dtypes may differ, e.g. an fp32
+    accumulator fed bf16 partials); lse_*: contiguous fp32 [...]."""
     D = o_acc.shape[-1]
     rows = o_acc.numel() // D
     if o_part.shape != o_acc.shape or lse_acc.numel() != rows or lse_part.numel() != rows:
         raise GAEError(1, "lse_merge_: shape mismatch")
-    if not (o_acc.is_contiguous() and o_part.is_contiguous()):
-        raise GAEError(1, "lse_merge_: outputs must be contiguous")
+    if not (o_acc.is_contiguous() and o_part.is_contiguous() and lse_acc.is_contiguous()
+            and lse_part.is_contiguous()):
+        raise GAEError(1, "lse_merge_: tensors must be contiguous")
     _check(lib().gae_lse_merge(o_acc.data_ptr(), lse_acc.data_ptr(), o_part.data_ptr(),
                                lse_part.data_ptr(), rows, D, D, D, _dtype_code(o_acc),
-                               _stream_ptr(stream)))
+                               _dtype_code(o_part), _stream_ptr(stream)))
     return o_acc, lse_acc
 
 

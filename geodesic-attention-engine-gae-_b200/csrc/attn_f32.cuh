@@ -131,8 +131,8 @@ template <> __device__ __forceinline__ float from_f<float>(float x) { return x; 
 template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
 template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
 
-template <typename T>
-__global__ void lse_merge_kernel(T *o_acc, float *lse_acc, const T *o_part, const float *lse_part,
+template <typename TA, typename TP>
+__global__ void lse_merge_kernel(TA *o_acc, float *lse_acc, const TP *o_part, const float *lse_part,
                                  int64_t rows, int D, int64_t sa, int64_t sp) {
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -142,10 +142,10 @@ __global__ void lse_merge_kernel(T *o_acc, float *lse_acc, const T *o_part, cons
     if (mx == -INFINITY) return;
     const float wa = expf(la - mx), wb = expf(lb - mx);
     const float s = wa + wb;
-    T *oa = o_acc + row * sa;
-    const T *op = o_part + row * sp;
+    TA *oa = o_acc + row * sa;
+    const TP *op = o_part + row * sp;
     for (int c = lane; c < D; c += 32)
-        oa[c] = from_f<T>((wa * to_f<T>(oa[c]) + wb * to_f<T>(op[c])) / s);
+        oa[c] = from_f<TA>((wa * to_f<TA>(oa[c]) + wb * to_f<TP>(op[c])) / s);
     if (lane == 0) lse_acc[row] = mx + logf(s);
 }
 

@@ -335,6 +335,30 @@ gae_status host_attention(const float *q, const float *k, const float *v, size_t
     return s;
 }
 
+template <typename TA>
+gae_status launch_merge(void *o_acc, float *lse_acc, const void *o_part, const float *lse_part,
+                        int64_t rows, int64_t D, int64_t sa, int64_t sp, gae_dtype pd, cudaStream_t st) {
+    const int warps = 8;
+    dim3 grid((unsigned)((rows + warps - 1) / warps));
+    switch (pd) {
+        case GAE_DTYPE_F32:
+            gae::lse_merge_kernel<TA, float><<<grid, warps * 32, 0, st>>>(
+                (TA *)o_acc, lse_acc, (const float *)o_part, lse_part, rows, (int)D, sa, sp);
+            break;
+        case GAE_DTYPE_BF16:
+            gae::lse_merge_kernel<TA, __nv_bfloat16><<<grid, warps * 32, 0, st>>>(
+                (TA *)o_acc, lse_acc, (const __nv_bfloat16 *)o_part, lse_part, rows, (int)D, sa, sp);
+            break;
+        case GAE_DTYPE_F16:
+            gae::lse_merge_kernel<TA, __half><<<grid, warps * 32, 0, st>>>(
+                (TA *)o_acc, lse_acc, (const __half *)o_part, lse_part, rows, (int)D, sa, sp);
+            break;
+        default: return fail(GAE_ERR_INVALID_ARG, "unknown part dtype");
+    }
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
 }  // namespace
 
 // ==================================================================== C ABI
@@ -407,32 +431,19 @@ gae_status gae_attn_fwd(const gae_attn_args *a, void *stream) {
 }
 
 gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part, const float *lse_part,
-                         int64_t rows, int64_t head_dim, int64_t sa, int64_t sp, gae_dtype dtype,
-                         void *stream) {
+                         int64_t rows, int64_t head_dim, int64_t sa, int64_t sp, gae_dtype ad,
+                         gae_dtype pd, void *stream) {
     if (rows == 0) return GAE_OK;
-    if (!o_acc || !lse_acc || !o_part || !lse_part || rows < 0 || head_dim < 1)
+    if (!o_acc || !lse_acc || !o_part || !lse_part || rows < 0 || head_dim < 1 || sa < head_dim ||
+        sp < head_dim)
         return fail(GAE_ERR_INVALID_ARG, "invalid lse_merge arguments");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int warps = 8;
-    dim3 grid((unsigned)((rows + warps - 1) / warps));
-    switch (dtype) {
-        case GAE_DTYPE_F32:
-            gae::lse_merge_kernel<float><<<grid, warps * 32, 0, st>>>(
-                (float *)o_acc, lse_acc, (const float *)o_part, lse_part, rows, (int)head_dim, sa, sp);
-            break;
-        case GAE_DTYPE_BF16:
-            gae::lse_merge_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(
-                (__nv_bfloat16 *)o_acc, lse_acc, (const __nv_bfloat16 *)o_part, lse_part, rows,
-                (int)head_dim, sa, sp);
-            break;
-        case GAE_DTYPE_F16:
-            gae::lse_merge_kernel<__half><<<grid, warps * 32, 0, st>>>(
-                (__half *)o_acc, lse_acc, (const __half *)o_part, lse_part, rows, (int)head_dim, sa, sp);
-            break;
-        default: return fail(GAE_ERR_INVALID_ARG, "unknown dtype");
+    switch (ad) {
+        case GAE_DTYPE_F32: return launch_merge<float>(o_acc, lse_acc, o_part, lse_part, rows, head_dim, sa, sp, pd, st);
+        case GAE_DTYPE_BF16: return launch_merge<__nv_bfloat16>(o_acc, lse_acc, o_part, lse_part, rows, head_dim, sa, sp, pd, st);
+        case GAE_DTYPE_F16: return launch_merge<__half>(o_acc, lse_acc, o_part, lse_part, rows, head_dim, sa, sp, pd, st);
     }
-    GAE_CUDA_TRY(cudaGetLastError());
-    return GAE_OK;
+    return fail(GAE_ERR_INVALID_ARG, "unknown acc dtype");
 }
 
 gae_status gae_attn_int8_fwd(const gae_attn_int8_args *a, void *stream) {

@@ -1,0 +1,171 @@
+"""Sequence-parallel exact causal attention over P GPUs (ring attention).
+
+A new component (the reference has no multi-GPU path): one process per GPU,
+torch.distributed over NCCL for the plumbing, the library's fused attention
+kernel (gae_attn_fwd with q_offset/kv_offset) for each block pair and its
+log-sum-exp merge kernel (gae_lse_merge) to combine partial results, the same
+algebra as the reference's (max, sum, acc) block merge
+(cuda_src/waller_operator_v2.cu:120-142).
+
+Layout.  Every rank holds a contiguous shard [B, H, S, D] of a sequence of
+length N = P*S (rank r owns positions [r*S, (r+1)*S)).  With
+balance="zigzag" (the default for causal attention) the shards are first
+re-dealt so that rank r owns chunks r and 2P-1-r of 2P equal chunks; every
+ring step then costs every rank the same two chunk-pairs of work, instead of
+rank r doing r+1/2 blocks of work under the contiguous layout.  The output is
+dealt back to the contiguous layout at the end.
+
+Ring step t (t = 0 .. P-1): rank r computes with the K/V of rank (r - t) mod P
+while it sends that block to rank r+1 and receives the next one from rank r-1
+(batch_isend_irecv on NCCL's stream, overlapped with the attention kernels on
+the compute stream).  K and V travel as one packed buffer; remote blocks land
+in this GPU's own memory before any kernel reads them.
+
+`attend` and `merge` are injectable so that the host logic can be exercised on
+CPU ranks (gloo) in tests; the product path uses the CUDA kernels and fails
+loudly without them.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+
+def _default_attend(q, k, v, causal, q_offset, kv_offset, scale):
+    from . import attention
+    return attention(q, k, v, causal=causal, q_offset=q_offset, kv_offset=kv_offset,
+                     scale=scale, return_lse=True)
+
+
+def _default_merge(o_acc, lse_acc, o_part, lse_part):
+    from . import lse_merge_
+    lse_merge_(o_acc, lse_acc, o_part, lse_part)
+
+
+def zigzag_owner(chunk: int, P: int) -> int:
+    """Rank that owns chunk `chunk` (of 2P) under the balanced layout."""
+    return chunk if chunk < P else 2 * P - 1 - chunk
+
+
+def _redeal(x, rank, P, group, to_zigzag: bool):
+    """Moves the two half-shards between the contiguous and zig-zag layouts.
+
+    Contiguous rank r holds chunks 2r, 2r+1; zig-zag rank r holds chunks
+    r, 2P-1-r.  Point-to-point exchange, 2 sends and 2 receives per rank."""
+    S = x.shape[2]
+    C = S // 2
+    out = torch.empty_like(x)
+    ops, local = [], []
+    if to_zigzag:
+        # send my contiguous chunks to their zig-zag owners
+        for i, ch in enumerate((2 * rank, 2 * rank + 1)):
+            dst = zigzag_owner(ch, P)
+            slot = 0 if ch < P else 1
+            src_view = x[:, :, i * C:(i + 1) * C].contiguous()
+            if dst == rank:
+                local.append((out[:, :, slot * C:(slot + 1) * C], src_view))
+            else:
+                ops.append(dist.P2POp(dist.isend, src_view, dst, group))
+        # receive my zig-zag chunks from their contiguous owners
+        recv = []
+        for slot, ch in enumerate((rank, 2 * P - 1 - rank)):
+            src = ch // 2
+            if src != rank:
+                buf = torch.empty_like(x[:, :, :C])
+                ops.append(dist.P2POp(dist.irecv, buf, src, group))
+                recv.append((out[:, :, slot * C:(slot + 1) * C], buf))
+    else:
+        for slot, ch in enumerate((rank, 2 * P - 1 - rank)):
+            dst = ch // 2
+            i = ch % 2
+            src_view = x[:, :, slot * C:(slot + 1) * C].contiguous()
+            if dst == rank:
+                local.append((out[:, :, i * C:(i + 1) * C], src_view))
+            else:
+                ops.append(dist.P2POp(dist.isend, src_view, dst, group))
+        recv = []
+        for i, ch in enumerate((2 * rank, 2 * rank + 1)):
+            src = zigzag_owner(ch, P)
+            if src != rank:
+                buf = torch.empty_like(x[:, :, :C])
+                ops.append(dist.P2POp(dist.irecv, buf, src, group))
+                recv.append((out[:, :, i * C:(i + 1) * C], buf))
+    for dst_view, src_view in local:
+        dst_view.copy_(src_view)
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    for dst_view, buf in recv:
+        dst_view.copy_(buf)
+    return out
+
+
+def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "zigzag",
+                   scale: float | None = None, return_lse: bool = False, attend=None,
+                   merge=None):
+    """Exact attention of this rank's query shard against the whole sequence.
+
+    q, k, v: this rank's contiguous shard [B, H, S, D].  Returns the output
+    shard (dtype of q) and, with return_lse, the fp32 log-sum-exp [B, H, S].
+    """
+    attend = attend or _default_attend
+    merge = merge or _default_merge
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
+    B, H, S, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("ring_attention: q, k, v shards must have the same shape")
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    zig = causal and balance == "zigzag"
+    if zig and S % 2:
+        raise ValueError("ring_attention: zig-zag balance needs an even shard length")
+    if balance not in ("zigzag", "contiguous"):
+        raise ValueError(f"unknown balance {balance!r}")
+
+    # Local chunks: (global chunk id, offset in the local buffer, length).
+    if zig:
+        C = S // 2
+        q, k, v = (_redeal(t, r, P, group, True) if P > 1 else t for t in (q, k, v))
+        chunks_of = lambda rank: [(rank, 0, C), (2 * P - 1 - rank, C, C)]
+    else:
+        C = S
+        chunks_of = lambda rank: [(rank, 0, S)]
+
+    kv = torch.stack([k, v])  # one packed message per step
+    kv_next = torch.empty_like(kv) if P > 1 else None
+    acc = [None] * len(chunks_of(r))  # per local q chunk: (o fp32, lse)
+
+    for t in range(P):
+        src = (r - t) % P
+        reqs = []
+        if t < P - 1:
+            ops = [dist.P2POp(dist.isend, kv, (r + 1) % P, group),
+                   dist.P2POp(dist.irecv, kv_next, (r - 1) % P, group)]
+            reqs = dist.batch_isend_irecv(ops)
+        for qi, (qc, qo, ql) in enumerate(chunks_of(r)):
+            for kc, ko, kl in chunks_of(src):
+                if causal and kc > qc:
+                    continue  # every key after every query: fully masked
+                diag = causal and kc == qc
+                o_p, l_p = attend(q[:, :, qo:qo + ql], kv[0][:, :, ko:ko + kl],
+                                  kv[1][:, :, ko:ko + kl], diag, qc * C, kc * C, scale)
+                if acc[qi] is None:
+                    acc[qi] = (o_p.float().contiguous(), l_p.contiguous())
+                else:
+                    merge(acc[qi][0], acc[qi][1], o_p.contiguous(), l_p.contiguous())
+        for w in reqs:
+            w.wait()
+        if t < P - 1:
+            kv, kv_next = kv_next, kv
+
+    out = torch.empty_like(q)
+    lse = torch.empty((B, H, S), dtype=torch.float32, device=q.device)
+    for (qc, qo, ql), a in zip(chunks_of(r), acc):
+        out[:, :, qo:qo + ql] = a[0].to(out.dtype)
+        lse[:, :, qo:qo + ql] = a[1]
+    if zig and P > 1:
+        out = _redeal(out, r, P, group, False)
+        lse = _redeal(lse.unsqueeze(-1), r, P, group, False).squeeze(-1)
+    return (out, lse) if return_lse else out

@@ -178,13 +178,16 @@ GAE_API gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_
  * restated on normalised outputs): in place
  *   m = max(lse_acc, lse_part); a = e^(lse_acc-m); b = e^(lse_part-m)
  *   o_acc = (a*o_acc + b*o_part)/(a+b);  lse_acc = m + log(a+b).
- * o_acc/o_part: [rows, head_dim] with row stride (elements) of dtype;
- * lse: fp32 [rows] contiguous.  Rows with both lse = -inf are left as is.
+ * o_acc ([rows, head_dim], row stride o_acc_row_stride elements, type
+ * acc_dtype) and o_part (row stride o_part_row_stride, type part_dtype) may
+ * differ in type, e.g. an fp32 accumulator fed bf16 partials by a ring of
+ * sequence-parallel steps; lse: fp32 [rows] contiguous.  Rows with both
+ * lse = -inf are left as is.
  * ---------------------------------------------------------------------- */
 GAE_API gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part,
                          const float *lse_part, int64_t rows, int64_t head_dim,
                          int64_t o_acc_row_stride, int64_t o_part_row_stride,
-                         gae_dtype dtype, void *stream);
+                         gae_dtype acc_dtype, gae_dtype part_dtype, void *stream);
 
 /* ------------------------------------------------------------------------
  * Fused pre-norm transformer layer (replaces the fused "symphony" layer,
