@@ -28,7 +28,9 @@ from dataclasses import dataclass
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libgae.so")
+# GAE_LIB selects another build of the library (e.g. the diagnostics variant
+# lib/libgae_trace.so); the default is lib/libgae.so.
+LIB_PATH = os.environ.get("GAE_LIB") or os.path.join(_HERE, "lib", "libgae.so")
 
 GAE_OK = 0
 _STATUS = {0: "GAE_OK", 1: "GAE_ERR_INVALID_ARG", 2: "GAE_ERR_UNSUPPORTED", 3: "GAE_ERR_CUDA",
@@ -99,6 +101,7 @@ def lib():
     L.gae_layer_fwd.argtypes = [vp, vp, vp]
     L.gae_layer_stack_fwd.argtypes = [vp, vp, C.c_int, vp]
     L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
+    L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     _lib = L
     return L
 

@@ -40,12 +40,20 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(s) <= t for s in _sources())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
+TRACE_LIB_PATH = os.path.join(LIB_DIR, "libgae_trace.so")
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    """Builds lib/libgae.so, or with trace=True the diagnostics variant
+    lib/libgae_trace.so whose attention kernel records pipeline cycle stamps
+    (include/gae_debug.h)."""
+    out = TRACE_LIB_PATH if trace else LIB_PATH
+    if not force and not trace and up_to_date():
         return LIB_PATH
     os.makedirs(LIB_DIR, exist_ok=True)
-    tmp = LIB_PATH + ".tmp"
-    cmd = [NVCC, *NVCC_FLAGS, os.path.join(HERE, "csrc", "gae_abi.cu"), "-o", tmp]
+    tmp = out + ".tmp"
+    cmd = [NVCC, *NVCC_FLAGS, *(["-DGAE_ATTN_TRACE"] if trace else []),
+           os.path.join(HERE, "csrc", "gae_abi.cu"), "-o", tmp]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)
@@ -53,9 +61,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError("nvcc failed:\n" + res.stdout + res.stderr)
     if verbose:
         sys.stderr.write(res.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, trace="--trace" in sys.argv))

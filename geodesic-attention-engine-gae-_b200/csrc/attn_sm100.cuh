@@ -54,6 +54,32 @@ struct AttnParams {
     int64_t q_offset, kv_offset;
 };
 
+// Optional cycle-stamp trace of one CTA (diagnostics; see gae_debug.h).  When
+// gae_attn_trace is non-null, CTA (trace_cta, 0) records %clock64 at the
+// pipeline events below, indexed by K/V tile (up to kTraceTiles).
+constexpr int kTraceTiles = 256;
+enum TraceEvent : int {
+    kTrSWait0 = 0, kTrSWait1, kTrPDone0, kTrPDone1,  // softmax group g: S ready / P written
+    kTrMmaP0, kTrMmaP1, kTrMmaIssued0, kTrMmaIssued1,  // MMA warp: P_g seen / MMAs issued
+    kTrNumEvents
+};
+__device__ unsigned long long *gae_attn_trace = nullptr;
+__device__ int gae_attn_trace_cta = 0;
+#ifdef GAE_ATTN_TRACE
+#define GAE_TRACE(ev, tile)                                                     \
+    do {                                                                        \
+        if (trace && (tile) < kTraceTiles) trace[(ev) * kTraceTiles + (tile)] = clock64_now(); \
+    } while (0)
+#else
+#define GAE_TRACE(ev, tile) do { } while (0)
+#endif
+
+__device__ __forceinline__ unsigned long long clock64_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+    return t;
+}
+
 enum AttnWaitSite : unsigned {
     kSiteQ = 0x101,
     kSiteKvFull = 0x102,
@@ -121,6 +147,10 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
     volatile int no_abort = 0;  // for drains that must not be cut short
+#ifdef GAE_ATTN_TRACE
+    unsigned long long *trace =
+        (gae_attn_trace && blockIdx.x == gae_attn_trace_cta && blockIdx.y == 0) ? gae_attn_trace : nullptr;
+#endif
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
@@ -255,14 +285,17 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
                          mbar_wait(bar_p(0), (j - 1) & 1, kSiteP, abort_flag);
                     if (!ok) break;
+                    GAE_TRACE(kTrMmaP0, j - 1);
                     tc_fence_after();
                     issue_pv(0, v_slot, j - 1 > 0);
                 }
                 issue_qk(0, k_slot);
                 umma_commit(bar_s(0));
+                GAE_TRACE(kTrMmaIssued0, j);
                 if (j > 0) {
                     ok = mbar_wait(bar_p(1), (j - 1) & 1, kSiteP, abort_flag);
                     if (!ok) break;
+                    GAE_TRACE(kTrMmaP1, j - 1);
                     tc_fence_after();
                     issue_pv(1, v_slot, j - 1 > 0);
                     umma_commit(bar_kv_empty(v_slot));
@@ -272,6 +305,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 issue_qk(1, k_slot);
                 umma_commit(bar_s(1));
                 if (!Cfg::kInt8) umma_commit(bar_kv_empty(k_slot));
+                GAE_TRACE(kTrMmaIssued1, j);
             }
             if (ok) {
                 const int v_item = 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
@@ -323,6 +357,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         for (int j = 0; j < n_kv; ++j) {
             ok = mbar_wait(bar_s(grp), j & 1, kSiteS, abort_flag);
             if (!ok) break;
+            if (row == 0) GAE_TRACE(kTrSWait0 + grp, j);
             tc_fence_after();
             float s[128];
             {
@@ -437,6 +472,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar_p(grp));
+            if (row == 0) GAE_TRACE(kTrPDone0 + grp, j);
         }
 
         // Epilogue: O_i / l -> global; log-sum-exp.

@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "../../include/gae.h"
+#include "../../include/gae_debug.h"
 #include "attn_f32.cuh"
 #include "attn_sm100.cuh"
 #include "attn_int8_sm100.cuh"
@@ -396,6 +397,17 @@ gae_status gae_device_status(int reset) {
         GAE_CUDA_TRY(cudaMemcpyToSymbol(gae::gae_dev_error, &z, sizeof(z)));
     }
     if (v) return fail(GAE_ERR_TIMEOUT, "a device-side wait timed out (site 0x%x)", v);
+    return GAE_OK;
+}
+
+gae_status gae_debug_attn_trace(void *buf, int cta) {
+#ifndef GAE_ATTN_TRACE
+    (void)buf; (void)cta;
+    return fail(GAE_ERR_UNSUPPORTED, "this build has no attention trace (compile with -DGAE_ATTN_TRACE)");
+#endif
+    unsigned long long *p = static_cast<unsigned long long *>(buf);
+    GAE_CUDA_TRY(cudaMemcpyToSymbol(gae::gae_attn_trace, &p, sizeof(p)));
+    GAE_CUDA_TRY(cudaMemcpyToSymbol(gae::gae_attn_trace_cta, &cta, sizeof(cta)));
     return GAE_OK;
 }
 

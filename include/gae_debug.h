@@ -1,0 +1,34 @@
+/*
+ * gae_debug.h -- diagnostics of libgae.so (not part of the attention API).
+ *
+ * No counterpart in the reference project: these hooks exist to measure the
+ * tensor-core attention kernel's pipeline on the GPU.
+ */
+#ifndef GAE_DEBUG_H_
+#define GAE_DEBUG_H_
+
+#include "gae.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Number of events and K/V tiles per event in an attention trace buffer. */
+#define GAE_TRACE_EVENTS 8
+#define GAE_TRACE_TILES 256
+
+/* Arms (buf != NULL) or disarms (buf == NULL) the cycle-stamp trace of the
+ * tensor-core attention kernel on the current device: the CTA with
+ * blockIdx = (cta, 0) of every later launch writes %clock64 stamps into
+ * buf[event * GAE_TRACE_TILES + tile] (unsigned 64-bit, device memory of
+ * GAE_TRACE_EVENTS * GAE_TRACE_TILES entries).  Events: 0/1 softmax group
+ * 0/1 saw S, 2/3 group 0/1 published P, 4/5 MMA warp saw P of group 0/1,
+ * 6/7 MMA warp issued group 0/1's MMAs for that tile.  CTA index x counts
+ * from the heaviest query block (x = 0 is the last 256 query rows). */
+GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GAE_DEBUG_H_ */
