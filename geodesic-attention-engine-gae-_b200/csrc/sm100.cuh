@@ -244,6 +244,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
         : "memory");
 }
 
+// Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Warpgroup register re-balancing.  Executed by all warps of a warpgroup;
 // the shares must add up to the block's launch allocation.
 template <int N>
@@ -324,6 +329,41 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 2^x for a pair of x <= 2^22 on the FMA/ALU pipes instead of the MUFU,
+// following Cody and Waite's range reduction (W. J. Cody, W. Waite,
+// "Software Manual for the Elementary Functions", 1980): x = j + f with
+// j = floor(x) and f in [0, 1); 2^f by a degree-3 polynomial whose
+// coefficients are the minimax fit of 2^f on [0, 1) in relative error
+// (computed for this library by linear programming over 4001 points; max
+// relative error 7.5e-5, well below bf16's 2^-9); 2^j is added to the
+// exponent field.  floor(x) comes from one add rounding toward -inf with
+// 1.5 * 2^23, which leaves j in the low mantissa bits.  x is clamped at -126
+// so that the exponent field cannot underflow into the sign bit; results
+// there are below 2^-125 and vanish next to a row sum of at least 1.
+__device__ __forceinline__ void exp2_poly_x2(uint64_t x2, float &r0, float &r1) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    float x0, x1;
+    f2_unpack(x2, x0, x1);
+    x0 = fmaxf(x0, -126.f);
+    x1 = fmaxf(x1, -126.f);
+    const uint64_t xc = f2_pack(x0, x1);
+    const uint64_t mg = f2_pack(kMagic, kMagic);
+    uint64_t t, j, f;
+    asm("add.rm.f32x2 %0, %1, %2;" : "=l"(t) : "l"(xc), "l"(mg));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(j) : "l"(t), "l"(mg));
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(f) : "l"(xc), "l"(j));
+    uint64_t p = f2_fma(f, f2_pack(0.07802301f, 0.07802301f), f2_pack(0.22606939f, 0.22606939f));
+    p = f2_fma(p, f, f2_pack(0.69583285f, 0.69583285f));
+    p = f2_fma(p, f, f2_pack(0.99992526f, 0.99992526f));
+    float p0, p1, t0, t1;
+    f2_unpack(p, p0, p1);
+    f2_unpack(t, t0, t1);
+    // bits(t) * 2^23 puts j into the exponent field (the magic's own bits
+    // vanish modulo 2^32); adding bits(p) scales p by 2^j.
+    r0 = __uint_as_float(__float_as_uint(t0) * 8388608u + __float_as_uint(p0));
+    r1 = __uint_as_float(__float_as_uint(t1) * 8388608u + __float_as_uint(p1));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

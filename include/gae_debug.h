@@ -14,7 +14,7 @@ extern "C" {
 #endif
 
 /* Number of events and K/V tiles per event in an attention trace buffer. */
-#define GAE_TRACE_EVENTS 8
+#define GAE_TRACE_EVENTS 12
 #define GAE_TRACE_TILES 256
 
 /* Arms (buf != NULL) or disarms (buf == NULL) the cycle-stamp trace of the
@@ -23,7 +23,8 @@ extern "C" {
  * buf[event * GAE_TRACE_TILES + tile] (unsigned 64-bit, device memory of
  * GAE_TRACE_EVENTS * GAE_TRACE_TILES entries).  Events: 0/1 softmax group
  * 0/1 saw S, 2/3 group 0/1 published P, 4/5 MMA warp saw P of group 0/1,
- * 6/7 MMA warp issued group 0/1's MMAs for that tile.  CTA index x counts
+ * 6/7 MMA warp issued group 0/1's MMAs for that tile, 8/9 group 0/1 has
+ * S in registers, 10/11 group 0/1 has its row max.  CTA index x counts
  * from the heaviest query block (x = 0 is the last 256 query rows). */
 GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
 
