@@ -101,6 +101,7 @@ def lib():
     L.gae_layer_fwd.argtypes = [vp, vp, vp]
     L.gae_layer_stack_fwd.argtypes = [vp, vp, C.c_int, vp]
     L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
+    L.gae_linear_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     _lib = L
     return L
@@ -415,3 +416,159 @@ class TransformerConfig:
     @classmethod
     def from_gae(cls, cfg: GAEConfig):
         return cls(cfg.hidden_dim, cfg.num_heads, cfg.head_dim, cfg.mlp_dim, cfg.ln_eps)
+
+
+# ------------------------------------------------------ fused layer (GPU)
+EPI_BIAS, EPI_GELU, EPI_RESIDUAL = 0, 1, 2
+
+
+def linear(x, w, bias=None, res=None, gelu=False, out=None, stream=None):
+    """y = x @ w^T (+ bias) then tanh-GELU or + res; bf16 [M, K] x [N, K] on tcgen05.
+
+    The tensor-core replacement of the crate's matvecs (rust_src/src/mlp.rs:7-36,
+    transformer.rs:124-134): w is stored [out, in]."""
+    torch = _torch()
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise GAEError(1, "linear: w must be [N, K]")
+    for t in (x, w) + ((res,) if res is not None else ()):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise GAEError(1, "linear: x, w, res must be contiguous bf16")
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise GAEError(1, "linear: bias must be contiguous fp32")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    epi = EPI_GELU if gelu else (EPI_RESIDUAL if res is not None else EPI_BIAS)
+    _check(lib().gae_linear_fwd(x.data_ptr(), w.data_ptr(),
+                                bias.data_ptr() if bias is not None else None,
+                                res.data_ptr() if res is not None else None, out.data_ptr(),
+                                M, N, K, epi, _stream_ptr(stream)))
+    return out
+
+
+def layernorm_rows(x, gamma, beta, eps=1e-5, res=None, sum_out=None, out=None, stream=None):
+    """Row LayerNorm of bf16 [rows, d] (layernorm.rs:20-47 semantics): optional
+    fused residual add (the rounded sum is written to sum_out when given)."""
+    torch = _torch()
+    rows, d = x.shape
+    if out is None:
+        out = torch.empty_like(x)
+    _check(lib().gae_layernorm_fwd(x.data_ptr(), res.data_ptr() if res is not None else None,
+                                   sum_out.data_ptr() if sum_out is not None else None,
+                                   out.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, d,
+                                   float(eps), _stream_ptr(stream)))
+    return out
+
+
+class LayerArgs(C.Structure):
+    """Mirror of gae_layer_args (include/gae.h)."""
+    _fields_ = [("x", C.c_void_p), ("out", C.c_void_p), ("batch", C.c_int64), ("seq", C.c_int64),
+                ("d_model", C.c_int64), ("heads", C.c_int64), ("d_ff", C.c_int64),
+                ("eps", C.c_float), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t)]
+
+
+class LayerWeights(C.Structure):
+    """Mirror of gae_layer_weights (include/gae.h)."""
+    _fields_ = [(n, C.c_void_p) for n in (
+        "ln1_gamma", "ln1_beta", "w_qkv", "b_qkv", "w_proj", "b_proj", "ln2_gamma", "ln2_beta",
+        "w_fc", "b_fc", "w_fc2", "b_fc2")]
+
+
+class Gpt2Layer:
+    """One pre-norm GPT-2 layer on the device (gae_layer_fwd):
+    x1 = x + proj(attn(LN1(x))); out = x1 + fc2(gelu(fc1(LN2(x1)))).
+    Weights bf16 [out, in], biases and LN parameters fp32, all on the GPU."""
+    NAMES = ("ln1_gamma", "ln1_beta", "w_qkv", "b_qkv", "w_proj", "b_proj", "ln2_gamma",
+             "ln2_beta", "w_fc", "b_fc", "w_fc2", "b_fc2")
+
+    def __init__(self, d_model, heads, d_ff, weights: dict, eps=1e-5):
+        self.d_model, self.heads, self.d_ff, self.eps = d_model, heads, d_ff, eps
+        self.w = {n: weights[n].contiguous() for n in self.NAMES}
+        self._cw = LayerWeights(*(self.w[n].data_ptr() for n in self.NAMES))
+
+    @classmethod
+    def random(cls, d_model, heads, d_ff, device="cuda", seed=0, eps=1e-5):
+        """GPT-2-style init: weights N(0, 0.02), biases 0, LN gamma 1 / beta 0."""
+        torch = _torch()
+        g = torch.Generator().manual_seed(seed)
+        mk = lambda *s: (torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16).to(device)
+        z = lambda n: torch.zeros(n, dtype=torch.float32, device=device)
+        o = lambda n: torch.ones(n, dtype=torch.float32, device=device)
+        D, F = d_model, d_ff
+        return cls(D, heads, F, dict(ln1_gamma=o(D), ln1_beta=z(D), w_qkv=mk(3 * D, D),
+                                     b_qkv=z(3 * D), w_proj=mk(D, D), b_proj=z(D),
+                                     ln2_gamma=o(D), ln2_beta=z(D), w_fc=mk(F, D), b_fc=z(F),
+                                     w_fc2=mk(D, F), b_fc2=z(D)), eps)
+
+    def _args(self, x, out, ws):
+        B, S, D = x.shape
+        return LayerArgs(x.data_ptr(), out.data_ptr(), B, S, D, self.heads, self.d_ff, self.eps,
+                         ws.data_ptr(), ws.numel())
+
+    def workspace(self, B, S, device="cuda"):
+        torch = _torch()
+        n = lib().gae_layer_workspace_bytes(B, S, self.d_model, self.d_ff)
+        return torch.empty(n, dtype=torch.uint8, device=device)
+
+    def forward(self, x, out=None, workspace=None, stream=None):
+        """x: bf16 [B, S, d_model] contiguous; returns bf16 [B, S, d_model]."""
+        torch = _torch()
+        B, S, D = x.shape
+        out = torch.empty_like(x) if out is None else out
+        ws = self.workspace(B, S, x.device) if workspace is None else workspace
+        a = self._args(x, out, ws)
+        _check(lib().gae_layer_fwd(C.byref(a), C.byref(self._cw), _stream_ptr(stream)))
+        return out
+
+
+def layer_stack_forward(layers, x, out=None, workspace=None, stream=None):
+    """Applies layers (a list of Gpt2Layer of one shape) in order through
+    gae_layer_stack_fwd (one call, ping-pong buffers in the workspace)."""
+    torch = _torch()
+    B, S, D = x.shape
+    out = torch.empty_like(x) if out is None else out
+    ws = layers[0].workspace(B, S, x.device) if workspace is None else workspace
+    arr = (LayerWeights * len(layers))(*(l._cw for l in layers))
+    a = layers[0]._args(x, out, ws)
+    _check(lib().gae_layer_stack_fwd(C.byref(a), arr, len(layers), _stream_ptr(stream)))
+    return out
+
+
+class TransformerBlock:
+    """ate::TransformerBlock (rust_src/src/transformer.rs:36-120) on the GPU
+    kernels.  Weights keep the crate's layouts (wq/wk/wv/wo [h, h] as
+    W[out, in]; w1 [h, m]; w2 [m, h]); forward() reproduces the crate's demo
+    forward exactly as written (transformer.rs:87-120: per-token LN1 -> Wv ->
+    Wo + residual -> MLP + residual -> LN2, no cross-token attention) in bf16
+    on the tensor cores.  hidden_dim and mlp_dim must be multiples of 256."""
+
+    def __init__(self, config: TransformerConfig, **w):
+        self.config = config
+        for k, v in w.items():
+            setattr(self, k, np.asarray(v, np.float32))
+
+    @classmethod
+    def new_random(cls, config: TransformerConfig):
+        """transformer.rs:66-84: constant 0.02 weights, unit/zero LN parameters."""
+        h, m = config.hidden_dim, config.mlp_dim
+        f = lambda n, v: np.full(n, v, np.float32)
+        return cls(config, wq=f(h * h, .02), wk=f(h * h, .02), wv=f(h * h, .02),
+                   wo=f(h * h, .02), ln1_gamma=f(h, 1), ln1_beta=f(h, 0), w1=f(h * m, .02),
+                   b1=f(m, 0), w2=f(m * h, .02), b2=f(h, 0), ln2_gamma=f(h, 1), ln2_beta=f(h, 0))
+
+    def forward(self, input, seq_len: int):
+        torch = _torch()
+        cfg = self.config
+        h, m = cfg.hidden_dim, cfg.mlp_dim
+        dev = "cuda"
+        bf = lambda a, shape: torch.from_numpy(np.ascontiguousarray(a, np.float32).reshape(shape)).to(dev).to(torch.bfloat16)
+        fp = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+        x = bf(_host_f32(input, seq_len * h)[: seq_len * h], (seq_len, h))
+        n = layernorm_rows(x, fp(self.ln1_gamma), fp(self.ln1_beta), cfg.eps)
+        v = linear(n, bf(self.wv, (h, h)))
+        r1 = linear(v, bf(self.wo, (h, h)), res=x)
+        hid = linear(r1, bf(self.w1.reshape(h, m).T, (m, h)), bias=fp(self.b1), gelu=True)
+        mo = linear(hid, bf(self.w2.reshape(m, h).T, (h, m)), bias=fp(self.b2), res=r1)
+        out = layernorm_rows(mo, fp(self.ln2_gamma), fp(self.ln2_beta), cfg.eps)
+        return out.float().cpu().numpy().reshape(-1)

@@ -360,6 +360,166 @@ gae_status launch_merge(void *o_acc, float *lse_acc, const void *o_part, const f
     return GAE_OK;
 }
 
+
+// ------------------------------------------------------------ layer kernels
+// 2-D bf16 map over a row-major [rows, cols] matrix with row stride ld
+// elements, box {64, box_rows}, 128-byte swizzle (K-major GEMM operands).
+gae_status make_map_kmajor(CUtensorMap *m, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
+                           int box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return GAE_OK;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+gae_status launch_linear(const void *x, int64_t ldx, const void *w, const float *bias, const void *res,
+                         int64_t ldr, void *y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epi,
+                         cudaStream_t st) {
+    using Cfg = gae::LinearCfg;
+    if (M < 0 || N < 1 || K < 1) return fail(GAE_ERR_INVALID_ARG, "invalid linear shape");
+    if (M == 0) return GAE_OK;
+    if (N % Cfg::BN != 0 || K % Cfg::BK != 0)
+        return fail(GAE_ERR_UNSUPPORTED, "linear needs N %% 256 == 0 and K %% 64 == 0 (N=%lld K=%lld)",
+                    (long long)N, (long long)K);
+    if (!x || !w || !y) return fail(GAE_ERR_INVALID_ARG, "NULL pointer");
+    if (epi == gae::kEpiBiasResidual && !res) return fail(GAE_ERR_INVALID_ARG, "residual epilogue needs res");
+    if (epi < 0 || epi > 2) return fail(GAE_ERR_INVALID_ARG, "unknown epilogue %d", epi);
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (res && !aligned16(res)) || (bias && !aligned16(bias)))
+        return fail(GAE_ERR_INVALID_ARG, "linear operands must be 16-byte aligned");
+    if (ldx % 8 || ldy % 8 || (res && ldr % 8))
+        return fail(GAE_ERR_INVALID_ARG, "row strides must be multiples of 8 elements");
+    gae::LinearParams p;
+    memset(&p, 0, sizeof(p));
+    gae_status s;
+    if ((s = make_map_kmajor(&p.tm_a, x, M, K, ldx, Cfg::BM)) != GAE_OK) return s;
+    if ((s = make_map_kmajor(&p.tm_b, w, N, K, K, Cfg::BN)) != GAE_OK) return s;
+    p.y = static_cast<__nv_bfloat16 *>(y);
+    p.bias = bias;
+    p.res = static_cast<const __nv_bfloat16 *>(res);
+    p.M = (int)M; p.N = (int)N; p.K = (int)K;
+    p.ldy = ldy; p.ldr = ldr;
+    p.epi = epi;
+    p.tiles_m = (int)((M + Cfg::BM - 1) / Cfg::BM);
+    p.tiles_n = (int)(N / Cfg::BN);
+    const int tiles = p.tiles_m * p.tiles_n;
+    if ((s = set_smem(gae::linear_kernel, Cfg::kSmemBytes)) != GAE_OK) return s;
+    const int grid = tiles < num_sms() ? tiles : num_sms();
+    gae::linear_kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(p);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status launch_layernorm(const void *x, const void *res, void *sum_out, void *y, const float *g,
+                            const float *b, int64_t rows, int64_t d, float eps, cudaStream_t st) {
+    if (rows == 0) return GAE_OK;
+    if (!x || !y || !g || !b || rows < 0) return fail(GAE_ERR_INVALID_ARG, "invalid layernorm arguments");
+    if (d % 8 != 0 || d > 8 * 32 * gae::kLnMaxChunks)
+        return fail(GAE_ERR_UNSUPPORTED, "layernorm needs d %% 8 == 0 and d <= 4096");
+    if (!aligned16(x) || !aligned16(y) || !aligned16(g) || !aligned16(b) || (res && !aligned16(res)) ||
+        (sum_out && !aligned16(sum_out)))
+        return fail(GAE_ERR_INVALID_ARG, "layernorm operands must be 16-byte aligned");
+    const int warps = 8;
+    dim3 grid((unsigned)((rows + warps - 1) / warps));
+    gae::layernorm_kernel<<<grid, warps * 32, 0, st>>>(
+        (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)res, (__nv_bfloat16 *)sum_out,
+        (__nv_bfloat16 *)y, g, b, rows, (int)d, eps);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+// Workspace carve-up of one layer (bytes, each region 256-byte aligned):
+// ln [T, D], qkv [T, 3D], attn [T, D], x1 [T, D], hidden [T, F], and for the
+// stack one spare activation [T, D].
+struct LayerWs {
+    size_t ln, qkv, attn, x1, hid, spare, total;
+};
+LayerWs layer_ws(int64_t T, int64_t D, int64_t F) {
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    LayerWs w;
+    size_t o = 0;
+    w.ln = o; o += al(T * D * 2);
+    w.qkv = o; o += al(T * 3 * D * 2);
+    w.attn = o; o += al(T * D * 2);
+    w.x1 = o; o += al(T * D * 2);
+    w.hid = o; o += al(T * F * 2);
+    w.spare = o; o += al(T * D * 2);
+    w.total = o;
+    return w;
+}
+
+gae_status layer_once(const gae_layer_args *a, const gae_layer_weights *w, const void *x, void *out,
+                      cudaStream_t st) {
+    const int64_t B = a->batch, S = a->seq, D = a->d_model, Hh = a->heads, F = a->d_ff, T = B * S;
+    const LayerWs L = layer_ws(T, D, F);
+    char *ws = static_cast<char *>(a->workspace);
+    void *ln = ws + L.ln, *qkv = ws + L.qkv, *att = ws + L.attn, *x1 = ws + L.x1, *hid = ws + L.hid;
+    gae_status s;
+    if ((s = launch_layernorm(x, nullptr, nullptr, ln, (const float *)w->ln1_gamma, (const float *)w->ln1_beta,
+                              T, D, a->eps, st)) != GAE_OK) return s;
+    if ((s = launch_linear(ln, D, w->w_qkv, (const float *)w->b_qkv, nullptr, 0, qkv, 3 * D, T, 3 * D, D,
+                           gae::kEpiBias, st)) != GAE_OK) return s;
+    // Causal attention straight from the packed qkv rows: head h of q/k/v is
+    // columns [h*hd, (h+1)*hd) of each third; O lands in [T, D] head-major.
+    const int64_t hd = D / Hh;
+    gae_attn_args at;
+    memset(&at, 0, sizeof(at));
+    at.q = qkv;
+    at.k = static_cast<char *>(qkv) + D * 2;
+    at.v = static_cast<char *>(qkv) + 2 * D * 2;
+    at.o = att;
+    at.batch = B; at.heads = Hh; at.seq_q = S; at.seq_kv = S; at.head_dim = hd;
+    const int64_t qs[3] = {S * 3 * D, hd, 3 * D}, os[3] = {S * D, hd, D};
+    memcpy(at.q_stride, qs, sizeof qs); memcpy(at.k_stride, qs, sizeof qs);
+    memcpy(at.v_stride, qs, sizeof qs); memcpy(at.o_stride, os, sizeof os);
+    at.dtype = GAE_DTYPE_BF16;
+    at.causal = 1;
+    at.scale = 1.0f / sqrtf((float)hd);
+    if ((s = launch_attn_tc(&at, st)) != GAE_OK) return s;
+    if ((s = launch_linear(att, D, w->w_proj, (const float *)w->b_proj, x, D, x1, D, T, D, D,
+                           gae::kEpiBiasResidual, st)) != GAE_OK) return s;
+    if ((s = launch_layernorm(x1, nullptr, nullptr, ln, (const float *)w->ln2_gamma, (const float *)w->ln2_beta,
+                              T, D, a->eps, st)) != GAE_OK) return s;
+    if ((s = launch_linear(ln, D, w->w_fc, (const float *)w->b_fc, nullptr, 0, hid, F, T, F, D,
+                           gae::kEpiBiasGelu, st)) != GAE_OK) return s;
+    return launch_linear(hid, F, w->w_fc2, (const float *)w->b_fc2, x1, D, out, D, T, D, F,
+                         gae::kEpiBiasResidual, st);
+}
+
+gae_status check_layer(const gae_layer_args *a, const gae_layer_weights *w) {
+    if (!a || !w) return fail(GAE_ERR_INVALID_ARG, "args or weights NULL");
+    if (a->batch < 1 || a->seq < 1 || a->d_model < 1 || a->heads < 1 || a->d_ff < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid layer shape");
+    if (a->d_model % a->heads) return fail(GAE_ERR_INVALID_ARG, "d_model must be divisible by heads");
+    const int64_t hd = a->d_model / a->heads;
+    if (hd != 64 && hd != 128) return fail(GAE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+    if (!a->x || !a->out || !a->workspace) return fail(GAE_ERR_INVALID_ARG, "NULL activation or workspace");
+    const LayerWs L = layer_ws(a->batch * a->seq, a->d_model, a->d_ff);
+    if (a->workspace_bytes < L.total)
+        return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", a->workspace_bytes, L.total);
+    const void *ps[12] = {w->ln1_gamma, w->ln1_beta, w->w_qkv, w->b_qkv, w->w_proj, w->b_proj,
+                          w->ln2_gamma, w->ln2_beta, w->w_fc, w->b_fc, w->w_fc2, w->b_fc2};
+    for (const void *q : ps)
+        if (!q) return fail(GAE_ERR_INVALID_ARG, "NULL layer weight");
+    return GAE_OK;
+}
 }  // namespace
 
 // ==================================================================== C ABI
@@ -458,6 +618,49 @@ gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part, const 
     return fail(GAE_ERR_INVALID_ARG, "unknown acc dtype");
 }
 
+size_t gae_layer_workspace_bytes(int64_t batch, int64_t seq, int64_t d_model, int64_t d_ff) {
+    if (batch < 1 || seq < 1 || d_model < 1 || d_ff < 1) return 0;
+    return layer_ws(batch * seq, d_model, d_ff).total;
+}
+
+gae_status gae_layer_fwd(const gae_layer_args *a, const gae_layer_weights *w, void *stream) {
+    gae_status s = check_layer(a, w);
+    if (s != GAE_OK) return s;
+    return layer_once(a, w, a->x, a->out, static_cast<cudaStream_t>(stream));
+}
+
+gae_status gae_layer_stack_fwd(const gae_layer_args *a, const gae_layer_weights *w, int n_layers,
+                               void *stream) {
+    gae_status s = check_layer(a, w);
+    if (s != GAE_OK) return s;
+    if (n_layers < 1) return fail(GAE_ERR_INVALID_ARG, "n_layers must be >= 1");
+    for (int i = 0; i < n_layers; ++i)
+        if ((s = check_layer(a, w + i)) != GAE_OK) return s;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const LayerWs L = layer_ws(a->batch * a->seq, a->d_model, a->d_ff);
+    void *spare = static_cast<char *>(a->workspace) + L.spare;
+    // Layer i reads cur and writes out when n_layers-1-i is even, else the
+    // spare buffer, so the last layer lands in out.  A layer may run in place
+    // (its input is last read by the projection, before its output is written).
+    const void *cur = a->x;
+    for (int i = 0; i < n_layers; ++i) {
+        void *nxt = ((n_layers - 1 - i) % 2 == 0) ? a->out : spare;
+        if ((s = layer_once(a, w + i, cur, nxt, st)) != GAE_OK) return s;
+        cur = nxt;
+    }
+    return GAE_OK;
+}
+
+gae_status gae_layernorm_fwd(const void *x, const void *res, void *sum_out, void *y, const float *gamma,
+                             const float *beta, int64_t rows, int64_t d, float eps, void *stream) {
+    return launch_layernorm(x, res, sum_out, y, gamma, beta, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+gae_status gae_linear_fwd(const void *x, const void *w, const float *bias, const void *res, void *y,
+                          int64_t M, int64_t N, int64_t K, int epilogue, void *stream) {
+    return launch_linear(x, K, w, bias, res, N, y, N, M, N, K, epilogue, static_cast<cudaStream_t>(stream));
+}
+
 gae_status gae_attn_int8_fwd(const gae_attn_int8_args *a, void *stream) {
     if (!a) return fail(GAE_ERR_INVALID_ARG, "args is NULL");
     if (a->batch_heads < 1 || a->seq < 0 || a->head_dim < 1)
@@ -495,20 +698,3 @@ gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, 
 }
 
 }  // extern "C"
-
-// ------------------------------------------------------------------------
-// Entry points whose kernels are not in this build yet: they validate nothing
-// and report GAE_ERR_UNSUPPORTED so that a caller fails loudly.
-extern "C" {
-size_t gae_layer_workspace_bytes(int64_t, int64_t, int64_t, int64_t) { return 0; }
-gae_status gae_layer_fwd(const gae_layer_args *, const gae_layer_weights *, void *) {
-    return fail(GAE_ERR_UNSUPPORTED, "gae_layer_fwd: not built");
-}
-gae_status gae_layer_stack_fwd(const gae_layer_args *, const gae_layer_weights *, int, void *) {
-    return fail(GAE_ERR_UNSUPPORTED, "gae_layer_stack_fwd: not built");
-}
-gae_status gae_layernorm_fwd(const void *, const void *, void *, void *, const float *,
-                             const float *, int64_t, int64_t, float, void *) {
-    return fail(GAE_ERR_UNSUPPORTED, "gae_layernorm_fwd: not built");
-}
-}

@@ -229,6 +229,15 @@ GAE_API gae_status gae_layer_fwd(const gae_layer_args *args, const gae_layer_wei
 GAE_API gae_status gae_layer_stack_fwd(const gae_layer_args *args, const gae_layer_weights *w,
                                int n_layers, void *stream);
 
+/* One linear layer of the fused layer, exposed for callers and tests:
+ * y[M, N] = x[M, K] @ w[N, K]^T + bias, then per `epilogue`: 0 nothing,
+ * 1 tanh-GELU (rust_src/src/activations.rs:5-7), 2 + res[M, N].  bf16 x, w,
+ * res, y (row-major, contiguous rows), fp32 bias (may be NULL); N % 256 == 0,
+ * K % 64 == 0.  Replaces the matvecs of rust_src/src/mlp.rs:7-36 and
+ * transformer.rs:124-134 with a tcgen05 GEMM. */
+GAE_API gae_status gae_linear_fwd(const void *x, const void *w, const float *bias, const void *res,
+                                  void *y, int64_t M, int64_t N, int64_t K, int epilogue, void *stream);
+
 /* Row LayerNorm with the reference's semantics (population variance, eps
  * inside the sqrt; rust_src/src/layernorm.rs:20-47): bf16 in/out, fp32
  * gamma/beta, optional fused residual add (res may be NULL: y = LN(x);
