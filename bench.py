@@ -10,6 +10,14 @@ Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
   ring           config 5, causal: one sequence of N=1,048,576 (H=8, head_dim=128)
                  sharded over the N GPUs (contiguous N/P shards, ring attention with
                  zig-zag balance, K/V rotated by NCCL send/recv; strong scaling)
+  int8           config 3: B=1, H=32, N=16384, head_dim=128, non-causal; Q, K
+                 quantised per row to int8 (fp32 scales), V bf16; QK^T on the int8
+                 tensor cores (int32 accumulation), P*V in bf16.  Ops counted as
+                 4*d per pair like the bf16 path.
+  gpt2           config 4: 12 pre-norm GPT-2-small layers (d_model 768, 12 x 64
+                 heads, MLP 3072, causal), B=8, seq=2048, weights N(0, 0.02); one
+                 step = the whole stack (gae_layer_stack_fwd, replayed as a CUDA
+                 graph); FLOPs = GEMMs 2*T*768*9216 + causal attention per layer.
 One step = one fused attention forward over the whole batch.  FLOPs count only
 visible (unmasked) score entries: 4*d per (query, key) pair, causal pairs
 N(N+1)/2 per head.  Inputs (3 x 128 MiB for mha) exceed the 126 MB L2, so no
@@ -45,6 +53,9 @@ WORKLOADS = {
     "mha-noncausal": dict(B=4, H=16, N=8192, D=128, causal=False, cfg="config2-noncausal"),
     "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
     "ring": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M", ring=True),
+    "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
+    "gpt2": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-gpt2-small-12L", gpt2=True,
+                 layers=12, d_model=768, d_ff=3072),
 }
 METRIC = "fused-attention TFLOPS (bf16 d=128)"
 
@@ -154,6 +165,34 @@ def cpu_sample(w, slices=8, rows_cap=None):
     from oracle import oracle
     N, D = w["N"], w["D"]
     rng = np.random.default_rng(1234)
+    if w.get("gpt2"):
+        # one layer of one sequence (batch 1 of the workload's B), full length
+        Dm, F, H = w["d_model"], w["d_ff"], w["H"]
+        x = rng.standard_normal((N, Dm)).astype(np.float32)
+        mk = lambda *sh: (rng.standard_normal(sh) * 0.02).astype(np.float32)
+        wts = dict(ln1_g=np.ones(Dm, np.float32), ln1_b=np.zeros(Dm, np.float32),
+                   wqkv=mk(Dm, 3 * Dm), bqkv=np.zeros(3 * Dm, np.float32), wproj=mk(Dm, Dm),
+                   bproj=np.zeros(Dm, np.float32), ln2_g=np.ones(Dm, np.float32),
+                   ln2_b=np.zeros(Dm, np.float32), wfc=mk(Dm, F), bfc=np.zeros(F, np.float32),
+                   wfc2=mk(F, Dm), bfc2=np.zeros(Dm, np.float32))
+        oracle.lib()
+        t0 = time.perf_counter()
+        oracle.gpt2_layer(x, 1, N, Dm, H, F, 1e-5, wts, round_bf16=False)
+        dt = time.perf_counter() - t0
+        flops = 2.0 * N * Dm * (4 * Dm + 2 * F) + attn_flops(1, H, N, N, D, True)
+        return flops / dt / 1e12, dt, f"one layer of one {N}-token sequence (fp32 oracle)", oracle.num_threads()
+    if w.get("int8"):
+        n_rows = N if rows_cap is None else min(N, rows_cap)
+        rows = None if n_rows == N else np.linspace(0, N - 1, n_rows).round().astype(np.int64)
+        q, sq = oracle.quantize_rows_int8(rng.standard_normal((slices, N, D)).astype(np.float32))
+        k, sk = oracle.quantize_rows_int8(rng.standard_normal((slices, N, D)).astype(np.float32))
+        v = rng.standard_normal((slices, N, D)).astype(np.float32)
+        t0 = time.perf_counter()
+        oracle.attention_int8(q, k, sq, sk, v, 1.0 / math.sqrt(D), causal=w["causal"], rows=rows)
+        dt = time.perf_counter() - t0
+        flops = 4.0 * D * n_rows * N * slices
+        return (flops / dt / 1e12, dt, f"{slices} head(s) x {n_rows} query rows, full key range each",
+                oracle.num_threads())
     q, k, v = (rng.standard_normal((1, slices, N, D)).astype(np.float32) for _ in range(3))
     n_rows = N if rows_cap is None else min(N, rows_cap)
     rows = None if n_rows == N else np.linspace(0, N - 1, n_rows).round().astype(np.int64)
@@ -179,6 +218,14 @@ def run_reference(args, w):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    if w.get("gpt2"):
+        vals, secs = [], []
+        for _ in range(args.warmup):
+            cpu_sample(w)
+        for _ in range(min(args.steps, 5)):
+            v, s, desc, threads = cpu_sample(w)
+            vals.append(v); secs.append(s)
+        return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
     # Calibrate: seconds per row of one slice (full key range).
     _, s_cal, _, _ = cpu_sample(w, slices=1, rows_cap=256)
     per_row = s_cal / 256
@@ -192,11 +239,14 @@ def run_reference(args, w):
         v, s, desc, threads = cpu_sample(w, slices=1, rows_cap=rows_cap)
         vals.append(v)
         secs.append(s)
-    value = statistics.mean(vals)
+    return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
+
+
+def _print_reference(args, w, value, sec, desc, threads):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000 * statistics.mean(secs), "higher_is_better": True,
+        "ms_per_step": 1000 * sec, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": w["cfg"], "B": w["B"], "H": w["H"], "seq_len": w["N"],
                    "head_dim": w["D"], "causal": w["causal"]},
@@ -251,7 +301,46 @@ def main():
     B, H, N, D, causal = w["B"], w["H"], w["N"], w["D"], w["causal"]
     is_ring = bool(w.get("ring"))
     stream = torch.cuda.current_stream()
-    if is_ring:
+    is_int8 = bool(w.get("int8"))
+    is_gpt2 = bool(w.get("gpt2"))
+    if is_gpt2:
+        T = B * N
+        L = w["layers"]
+        gemm = 2.0 * T * w["d_model"] * (3 * w["d_model"] + w["d_model"] + 2 * w["d_ff"])
+        flops = L * (gemm + attn_flops(B, H, N, N, D, True))
+        layers = [gae.Gpt2Layer.random(w["d_model"], H, w["d_ff"], device=dev, seed=100 + i)
+                  for i in range(L)]
+        g = torch.Generator(device="cpu").manual_seed(1000 + rank)
+        q = torch.randn(B, N, w["d_model"], generator=g).to(torch.bfloat16).to(dev)
+        k = v = q  # e2e copies only the input activations
+        out = torch.empty_like(q)
+        ws = layers[0].workspace(B, N, dev)
+        graph_in = torch.empty_like(q)
+        graph = torch.cuda.CUDAGraph()
+        gae.layer_stack_forward(layers, q, out=out, workspace=ws)  # warm the launch path
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            gae.layer_stack_forward(layers, graph_in, out=out, workspace=ws)
+
+        def run_step(q, k, v):
+            if q.data_ptr() != graph_in.data_ptr():
+                graph_in.copy_(q, non_blocking=True)
+            graph.replay()
+    elif is_int8:
+        gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
+        xq = torch.randn(B * H, N, D, generator=gen).to(dev)
+        xk = torch.randn(B * H, N, D, generator=gen).to(dev)
+        v = torch.randn(B * H, N, D, generator=gen).to(torch.bfloat16).to(dev)
+        qi, qs = gae.quantize_rows_int8(xq)
+        ki, ks = gae.quantize_rows_int8(xk)
+        del xq, xk
+        out = torch.empty_like(v)
+        flops = attn_flops(B, H, N, N, D, causal)
+        q, k = (qi, qs), (ki, ks)
+
+        def run_step(q, k, v):
+            gae.attention_int8(q[0], k[0], q[1], k[1], v, causal=causal, out=out)
+    elif is_ring:
         from gae_b200 import ring
         S = N // world
         ws = dict(w, N=S)
@@ -291,18 +380,28 @@ def main():
 
     # kernels of this library per step: the ring runs 3 block pairs + 1 merge at
     # P=1 and 2 pairs + 2 merges per further step (zig-zag balance).
-    launches_per_step = 4 + 4 * (world - 1)
+    launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
 
     # ---- end to end through the public API with host buffers ---------------
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    def flat(t):
+        return list(t) if isinstance(t, tuple) else [t]
+
+    inputs = flat(q) + ([] if is_gpt2 else flat(k) + flat(v))
+    host_in = [t.cpu().pin_memory() for t in inputs]
+    dev_in = [torch.empty_like(t) for t in inputs]
     hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def regroup(ts):
+        if is_gpt2:
+            return ts[0], ts[0], ts[0]
+        if is_int8:
+            return (ts[0], ts[1]), (ts[2], ts[3]), ts[4]
+        return ts[0], ts[1], ts[2]
 
     def e2e_step():
-        dq.copy_(hq, non_blocking=True)
-        dk.copy_(hk, non_blocking=True)
-        dv.copy_(hv, non_blocking=True)
-        run_step(dq, dk, dv)
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        run_step(*regroup(dev_in))
         hout.copy_(out, non_blocking=True)
 
     for _ in range(2):
@@ -316,7 +415,7 @@ def main():
     barrier()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / e2e_steps
     e2e_value = world * flops / (e2e_ms * 1e-3) / 1e12
-    bytes_in = 3 * q.numel() * q.element_size()
+    bytes_in = sum(t.numel() * t.element_size() for t in inputs)
     bytes_out = out.numel() * out.element_size()
 
     if world > 1:
@@ -334,7 +433,10 @@ def main():
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=None if w["N"] <= 16384 else 2048)
+        if w.get("int8"):
+            v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=2, rows_cap=2048)
+        else:
+            v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=None if w["N"] <= 16384 else 2048)
         cpu = {"value": v_cpu, "unit": "TFLOPS", "cores": threads, "kind": "port",
                "sample": desc + f" ({s_cpu:.1f} s)"}
 
@@ -342,7 +444,7 @@ def main():
         "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong" if is_ring else "weak",
-        "vs_baseline": None, "dtype": "bf16",
+        "vs_baseline": None, "dtype": "int8+bf16" if is_int8 else "bf16",
         "data": "synthetic",
         "config": {"workload": w["cfg"], "B": B, "H": H, "seq_len": N, "head_dim": D,
                    "causal": causal, "global_batch": B if is_ring else B * world,
@@ -350,7 +452,7 @@ def main():
                    "l2": "inputs larger than L2 (no flush)"},
         "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,
                 "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps * (launches_per_step if is_ring else 1),
+        "gpu_launches": args.steps * launches_per_step,
         "roofline": roofline,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),

@@ -104,10 +104,17 @@ def test_gpt2_stack_and_in_place(gae, ora):
     layers = [gae.Gpt2Layer.random(D, H, F, seed=20 + i) for i in range(3)]
     x = _bf((B, S, D), 21)
     y = gae.layer_stack_forward(layers, x.cuda())
+    # The stack is exactly the layers applied one after another ...
+    seq = x.cuda()
+    for l in layers:
+        seq = l.forward(seq)
+    assert torch.equal(seq.cpu(), y.cpu())
+    # ... and tracks the oracle within the per-layer tolerance times the depth
+    # (bf16 rounding differences compound from layer to layer).
     ref = x.float().numpy().reshape(B * S, D)
     for l in layers:
         ref = ora.gpt2_layer(ref, B, S, D, H, F, 1e-5, _oracle_weights(l), round_bf16=True)
-    assert within(y.float().cpu().numpy().reshape(B * S, D), ref) <= 2e-2
+    assert within(y.float().cpu().numpy().reshape(B * S, D), ref) <= 2e-2 * len(layers)
     # x and out may alias
     xd = x.cuda()
     gae.layer_stack_forward(layers, xd, out=xd)
