@@ -7,6 +7,7 @@ Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
   mha            BASELINE config 2, causal: B=4, H=16, N=8192, head_dim=128 (default)
   mha-noncausal  the same, non-causal
   long           config 5, causal: one sequence, H=8, head_dim=128, N=131072
+  mha64          the attention of config 4 alone: B=8, H=12, N=2048, head_dim=64, causal
   ring           config 5, causal: one sequence of N=1,048,576 (H=8, head_dim=128)
                  sharded over the N GPUs (contiguous N/P shards, ring attention with
                  zig-zag balance, K/V rotated by NCCL send/recv; strong scaling)
@@ -52,6 +53,7 @@ WORKLOADS = {
     "mha": dict(B=4, H=16, N=8192, D=128, causal=True, cfg="config2-causal"),
     "mha-noncausal": dict(B=4, H=16, N=8192, D=128, causal=False, cfg="config2-noncausal"),
     "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
+    "mha64": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-attention-d64"),
     "ring": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M", ring=True),
     "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
     "gpt2": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-gpt2-small-12L", gpt2=True,

@@ -123,6 +123,25 @@ struct AttnCfg {
     static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
+// Every kPeriod-th pair of probabilities can be computed by the polynomial
+// exp2 on the FMA pipe instead of the MUFU (0 = never).  Measured on B200:
+// the MUFU gives 4 ex2 per cycle per SM sub-partition and the polynomial 3.6
+// (issue-bound), and the two pipes run side by side.  At head_dim 128 the
+// tensor work per tile equals the MUFU work and moving pairs over did not
+// help; at head_dim 64 the tensor work per exponential is halved and the
+// kernel is MUFU-bound.
+#ifndef GAE_EMU_PERIOD_D128
+#define GAE_EMU_PERIOD_D128 0
+#endif
+#ifndef GAE_EMU_PERIOD_D64
+#define GAE_EMU_PERIOD_D64 3
+#endif
+template <int D>
+__device__ __forceinline__ constexpr bool use_poly_exp(int e) {
+    constexpr int kPeriod = (D == 64) ? GAE_EMU_PERIOD_D64 : GAE_EMU_PERIOD_D128;
+    return kPeriod > 0 && (e % (kPeriod > 0 ? kPeriod : 1)) == kPeriod - 1;
+}
+
 template <int D, int kMode>
 __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
     using Cfg = AttnCfg<D, kMode>;
@@ -440,9 +459,15 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const uint64_t x = f2_fma(f2_pack(s[c * 32 + 2 * e], s[c * 32 + 2 * e + 1]), sl2x2, negm2);
-                    float x0, x1;
-                    f2_unpack(x, x0, x1);
-                    const float p0 = ex2_approx(x0), p1 = ex2_approx(x1);
+                    float p0, p1;
+                    if (use_poly_exp<D>(e)) {
+                        exp2_poly_x2(x, p0, p1);  // this pair on the FMA pipe
+                    } else {
+                        float x0, x1;
+                        f2_unpack(x, x0, x1);
+                        p0 = ex2_approx(x0);
+                        p1 = ex2_approx(x1);
+                    }
                     acc2[e & 3] = f2_add(acc2[e & 3], f2_pack(p0, p1));
                     pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }

@@ -438,9 +438,18 @@ gae_status launch_layernorm(const void *x, const void *res, void *sum_out, void 
         return fail(GAE_ERR_INVALID_ARG, "layernorm operands must be 16-byte aligned");
     const int warps = 8;
     dim3 grid((unsigned)((rows + warps - 1) / warps));
-    gae::layernorm_kernel<<<grid, warps * 32, 0, st>>>(
-        (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)res, (__nv_bfloat16 *)sum_out,
-        (__nv_bfloat16 *)y, g, b, rows, (int)d, eps);
+    const int per_lane = (int)((d + 255) / 256);
+#define GAE_LN(K)                                                                                 \
+    gae::layernorm_kernel<K><<<grid, warps * 32, 0, st>>>(                                        \
+        (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)res, (__nv_bfloat16 *)sum_out,          \
+        (__nv_bfloat16 *)y, g, b, rows, (int)d, eps)
+    if (per_lane <= 1) GAE_LN(1);
+    else if (per_lane <= 2) GAE_LN(2);
+    else if (per_lane <= 3) GAE_LN(3);
+    else if (per_lane <= 4) GAE_LN(4);
+    else if (per_lane <= 8) GAE_LN(8);
+    else GAE_LN(16);
+#undef GAE_LN
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }

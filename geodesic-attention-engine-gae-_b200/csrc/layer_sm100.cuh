@@ -229,34 +229,46 @@ __global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ 
 // ------------------------------------------------------------- LayerNorm
 // One warp per row.  s = x (+ res, rounded to bf16 and written to sum_out);
 // y = (s - mean) / sqrt(var + eps) * gamma + beta with the population
-// variance; statistics in fp32 by two passes over registers.
+// variance; statistics in fp32 by two passes over registers.  kPerLane
+// 16-byte chunks per lane (d <= 256 * kPerLane) are held in registers, so the
+// instantiation is picked by row width to keep registers low and many rows in
+// flight per SM (the kernel is HBM-bound).
 constexpr int kLnMaxChunks = 16;  // 16 x 8 x 32 = 4096 elements per row at most
 
-__global__ void layernorm_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *res,
-                                 __nv_bfloat16 *sum_out, __nv_bfloat16 *y, const float *gamma,
-                                 const float *beta, int64_t rows, int D, float eps) {
+template <int kPerLane>
+__global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *res,
+                                                        __nv_bfloat16 *sum_out, __nv_bfloat16 *y,
+                                                        const float *gamma, const float *beta,
+                                                        int64_t rows, int D, float eps) {
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
     const int chunks = D / 8;  // 16-byte chunks per row
     const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * D);
     const uint4 *rr = res ? reinterpret_cast<const uint4 *>(res + row * D) : nullptr;
-    float v[kLnMaxChunks][8];
-    float sum = 0.f;
+    uint4 raw[kPerLane], rraw[kPerLane];
 #pragma unroll
-    for (int i = 0; i < kLnMaxChunks; ++i) {
+    for (int i = 0; i < kPerLane; ++i) {
         const int c = lane + 32 * i;
         if (c < chunks) {
-            const uint4 a = xr[c];
-            const uint32_t wa[4] = {a.x, a.y, a.z, a.w};
+            raw[i] = xr[c];
+            if (rr) rraw[i] = rr[c];
+        }
+    }
+    float v[kPerLane][8];
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPerLane; ++i) {
+        const int c = lane + 32 * i;
+        if (c < chunks) {
+            const uint32_t wa[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 v[i][2 * u] = __uint_as_float(wa[u] << 16);
                 v[i][2 * u + 1] = __uint_as_float(wa[u] & 0xffff0000u);
             }
             if (rr) {
-                const uint4 b = rr[c];
-                const uint32_t wb[4] = {b.x, b.y, b.z, b.w};
+                const uint32_t wb[4] = {rraw[i].x, rraw[i].y, rraw[i].z, rraw[i].w};
                 uint32_t pk[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -277,7 +289,7 @@ __global__ void layernorm_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *re
     const float mean = sum / (float)D;
     float sq = 0.f;
 #pragma unroll
-    for (int i = 0; i < kLnMaxChunks; ++i)
+    for (int i = 0; i < kPerLane; ++i)
         if (lane + 32 * i < chunks) {
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
@@ -290,7 +302,7 @@ __global__ void layernorm_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *re
     const float rstd = 1.f / sqrtf(sq / (float)D + eps);
     uint4 *yr = reinterpret_cast<uint4 *>(y + row * D);
 #pragma unroll
-    for (int i = 0; i < kLnMaxChunks; ++i) {
+    for (int i = 0; i < kPerLane; ++i) {
         const int c = lane + 32 * i;
         if (c < chunks) {
             const float4 g0 = __ldg(reinterpret_cast<const float4 *>(gamma) + 2 * c);
