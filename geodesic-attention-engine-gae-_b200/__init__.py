@@ -100,6 +100,7 @@ def lib():
     L.gae_layer_workspace_bytes.argtypes = [i64, i64, i64, i64]
     L.gae_layer_fwd.argtypes = [vp, vp, vp]
     L.gae_layer_stack_fwd.argtypes = [vp, vp, C.c_int, vp]
+    L.gae_layer_fwd_static.argtypes = [vp, vp, vp]
     L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
     L.gae_linear_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]

@@ -707,3 +707,65 @@ gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, 
 }
 
 }  // extern "C"
+
+// ====================================================================
+// Allocation-free layer forward.
+//
+// Some callers cannot allocate device memory for the layer's workspace: code
+// running inside an allocator or memory-pool callback, plugins whose host
+// application owns every device allocation and forbids cudaMalloc, or
+// real-time paths where an allocation may block.  gae_layer_fwd_static runs
+// the same kernels as gae_layer_fwd but takes its workspace from a
+// file-scope device array of kStaticLayerWsBytes, which every GPU that loads
+// this library holds until the process exits.  It calls no cudaMalloc,
+// cudaFree or other allocating routine.
+namespace {
+
+constexpr size_t kStaticLayerWsBytes = 32ull << 20;  // 32 MiB per device
+static __device__ __align__(256) unsigned char g_layer_static_ws[kStaticLayerWsBytes];
+
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_ws_mu;
+void *g_static_ws_ptr[kStaticMaxDevices] = {};
+
+// Device address of the array on the current device.  Host code may not use
+// the array's name as a pointer (it is only a host-side stand-in), so the
+// address is looked up once per device, with that device current.
+gae_status static_ws_address(void **out) {
+    int dev = 0;
+    GAE_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kStaticMaxDevices)
+        return fail(GAE_ERR_UNSUPPORTED, "device index %d beyond %d", dev, kStaticMaxDevices);
+    std::lock_guard<std::mutex> lock(g_static_ws_mu);
+    if (!g_static_ws_ptr[dev]) {
+        void *p = nullptr;
+        GAE_CUDA_TRY(cudaGetSymbolAddress(&p, g_layer_static_ws));
+        if (!p) return fail(GAE_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
+        g_static_ws_ptr[dev] = p;
+    }
+    *out = g_static_ws_ptr[dev];
+    return GAE_OK;
+}
+
+}  // namespace
+
+extern "C" gae_status gae_layer_fwd_static(const gae_layer_args *a, const gae_layer_weights *w,
+                                           void *stream) {
+    if (!a) return fail(GAE_ERR_INVALID_ARG, "args is NULL");
+    if (a->batch < 1 || a->seq < 1 || a->d_model < 1 || a->d_ff < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid layer shape");
+    const size_t need = layer_ws(a->batch * a->seq, a->d_model, a->d_ff).total;
+    if (need > kStaticLayerWsBytes)
+        return fail(GAE_ERR_UNSUPPORTED,
+                    "gae_layer_fwd_static: this shape needs %zu bytes of workspace, above the "
+                    "fixed %zu-byte static workspace; use gae_layer_fwd with a caller workspace",
+                    need, kStaticLayerWsBytes);
+    void *ws = nullptr;
+    gae_status s = static_ws_address(&ws);
+    if (s != GAE_OK) return s;
+    gae_layer_args b = *a;
+    b.workspace = ws;
+    b.workspace_bytes = kStaticLayerWsBytes;
+    if ((s = check_layer(&b, w)) != GAE_OK) return s;
+    return layer_once(&b, w, b.x, b.out, static_cast<cudaStream_t>(stream));
+}

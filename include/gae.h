@@ -229,6 +229,23 @@ GAE_API gae_status gae_layer_fwd(const gae_layer_args *args, const gae_layer_wei
 GAE_API gae_status gae_layer_stack_fwd(const gae_layer_args *args, const gae_layer_weights *w,
                                int n_layers, void *stream);
 
+/* One layer exactly as gae_layer_fwd, for callers that cannot allocate device
+ * memory (allocator or memory-pool callbacks, plugins whose host owns every
+ * device allocation, real-time paths where cudaMalloc may block).  No
+ * counterpart in the reference.  The workspace fields of args are ignored: the
+ * layer's scratch lives in a fixed 32 MiB device array inside libgae.so that
+ * every GPU loading the library holds until exit.  Shapes whose
+ * gae_layer_workspace_bytes exceeds 32 MiB (e.g. about 1980 tokens at GPT-2
+ * small widths) return GAE_ERR_UNSUPPORTED.  Nothing is allocated; the first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture.  Every call shares the one
+ * array, which keeps the previous call's contents (the layer writes every
+ * workspace byte it reads, so nothing needs clearing); calls that overlap on
+ * the GPU (other streams, other threads) race on it and must be serialised by
+ * the caller. */
+GAE_API gae_status gae_layer_fwd_static(const gae_layer_args *args, const gae_layer_weights *w,
+                                        void *stream);
+
 /* One linear layer of the fused layer, exposed for callers and tests:
  * y[M, N] = x[M, K] @ w[N, K]^T + bias, then per `epilogue`: 0 nothing,
  * 1 tanh-GELU (rust_src/src/activations.rs:5-7), 2 + res[M, N].  bf16 x, w,
