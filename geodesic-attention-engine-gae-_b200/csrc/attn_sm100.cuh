@@ -8,16 +8,18 @@
 // .cu:40-290 (cuBLAS tiles, S/P round-trip HBM) and cuda_src/bench_tma.cu:152-
 // 429 (Hopper TMA + wgmma); this kernel is a new design for tcgen05/TMEM.
 //
-// CTA = 256 query rows of one (batch, head): two 128-row Q tiles that
-// ping-pong on the tensor core.  Warp roles (384 threads, 3 warpgroups):
+// Persistent CTAs (one per SM) walk a heaviest-first list of units; a unit is
+// 256 query rows of one (batch, head): two 128-row Q tiles that ping-pong on
+// the tensor core.  Warp roles (384 threads, 3 warpgroups):
 //   warps 0-3  softmax group 0  (Q tile 0, TMEM lanes 0..127, thread = row)
 //   warps 4-7  softmax group 1  (Q tile 1)
 //   warp  8    TMA producer     (Q once, then K_j, V_j into a smem ring)
 //   warp  9    MMA issuer       (owns the TMEM allocation)
 //   warps 10-11 idle
 // Registers: launched at 168 per thread; the producer warpgroup shrinks to
-// 72 and the two softmax warpgroups grow to 216 (2*128*216 + 128*72 =
-// 384*168, so the re-balancing always fits).
+// 80 (96 in int8 mode) and the two softmax warpgroups grow to 208 (200):
+// 2*128*208 + 128*80 and 2*128*200 + 128*96 are at most 384*168, so the
+// re-balancing always fits.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O0 [256,256+D), O1 after it.
 // P_i (bf16, 2 per column) overwrites the first 64 columns of S_i and feeds
 // the P*V MMA straight from TMEM.  Per K/V tile j the MMA warp issues
@@ -110,13 +112,15 @@ struct AttnCfg {
     static constexpr int kQBytes = 2 * kQTileBytes;
     static constexpr int kRingBytes = kStages * kSlotBytes;
     static constexpr int kBarOffset = kQBytes + kRingBytes;
-    // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done
-    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1;
+    // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done, q_empty
+    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1;  // + q_empty
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
     static constexpr int kThreads = 384;
-    static constexpr int kRegsSoftmax = 216, kRegsProducer = 72;
+    // The producer warps' unit loop needs more than 72 registers (96 with the
+    // int8 scale loads); the softmax warps take the rest.
+    static constexpr int kRegsSoftmax = kInt8 ? 200 : 208, kRegsProducer = kInt8 ? 96 : 80;
     static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsProducer <= kThreads * 168, "register split");
     static_assert(kInt8 ? (D == 128) : (D == 64 || D == 128), "unsupported head_dim");
     static_assert(kKTileBytes + kKScaleBytes <= kSlotBytes, "K slot too small");
@@ -162,6 +166,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     auto bar_p = [&](int i) { return sBar + 8u * (3 + 2 * Cfg::kStages + i); };
     auto bar_o = [&](int i) { return sBar + 8u * (5 + 2 * Cfg::kStages + i); };
     const uint32_t bar_done = sBar + 8u * (7 + 2 * Cfg::kStages);
+    const uint32_t bar_q_empty = sBar + 8u * (8 + 2 * Cfg::kStages);
     uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kBarOffset + Cfg::kNumBars * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
@@ -173,22 +178,43 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    const int qpair = p.n_qpairs - 1 - (int)blockIdx.x;  // heaviest (causal) first
-    const int bh = blockIdx.y;
-    const int b = bh / p.H, h = bh % p.H;
-    const int q0 = qpair * 256;
-
-    // Number of K/V tiles this CTA visits.
-    int n_kv = (p.Nkv + Cfg::kBlockN - 1) / Cfg::kBlockN;
-    if (p.causal) {
-        const int64_t last_q = p.q_offset + (int64_t)min(q0 + 255, p.Nq - 1);
-        const int64_t last_key = last_q - p.kv_offset;
-        if (last_key < 0) n_kv = 0;
-        else n_kv = (int)min64((int64_t)n_kv, last_key / Cfg::kBlockN + 1);
-    }
+    // Persistent schedule: the CTAs share out the list of (query pair,
+    // batch*head) units, ordered heaviest first (the last query pairs see the most keys under a causal
+    // mask).  TMEM, barriers and the K/V ring live across units; barrier
+    // phases follow running counters (tiles, ring items, active units) that
+    // every role advances identically.
+    const int BH = p.B * p.H;
+    const int n_units = p.n_qpairs * BH;
+    struct Unit { int q0, b, h, bh, n_kv; };
+    auto unit_at = [&](int u) {
+        Unit x;
+        const int qpair = p.n_qpairs - 1 - u / BH;
+        x.bh = u % BH;
+        x.b = x.bh / p.H;
+        x.h = x.bh % p.H;
+        x.q0 = qpair * 256;
+        int n = (p.Nkv + Cfg::kBlockN - 1) / Cfg::kBlockN;
+        if (p.causal) {
+            const int64_t last_q = p.q_offset + (int64_t)min(x.q0 + 255, p.Nq - 1);
+            const int64_t last_key = last_q - p.kv_offset;
+            n = (last_key < 0) ? 0 : (int)min64((int64_t)n, last_key / Cfg::kBlockN + 1);
+        }
+        x.n_kv = n;
+        return x;
+    };
+    // Serpentine assignment: in round k this CTA takes list entry
+    // k*G + c (k even) or k*G + G-1-c (k odd), so the CTA that takes the
+    // heaviest entry of one round takes the lightest of the next.
+    const int G = gridDim.x, cta = blockIdx.x;
+    auto unit_of = [&](int k) { return k * G + ((k & 1) ? (G - 1 - cta) : cta); };
+    // Does this CTA have any unit with keys to visit (then it needs TMEM)?
+    bool any_work = false;
+    for (int k = 0; k * G < n_units && !any_work; ++k)
+        if (unit_of(k) < n_units) any_work = unit_at(unit_of(k)).n_kv > 0;
 
     if (threadIdx.x == 0) {
         mbar_init(bar_q(), 1);
+        mbar_init(bar_q_empty, 1);
         for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(bar_kv_full(s), 1);
             mbar_init(bar_kv_empty(s), 1);
@@ -202,72 +228,80 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 9 && n_kv > 0) {
+    if (warp == 9 && any_work) {
         tmem_alloc(smem_u32(tmem_base_slot), Cfg::kTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = (n_kv > 0) ? *tmem_base_slot : 0u;
+    const uint32_t tmem = any_work ? *tmem_base_slot : 0u;
 
     if (warp >= 10) {
         regs_dec<Cfg::kRegsProducer>();
     } else if (warp == 8) {
         // ------------------------------------------------------ TMA producer
         regs_dec<Cfg::kRegsProducer>();
-        if (lane == 0 && n_kv > 0) {
+        if (lane == 0 && any_work) {
             tma_prefetch_desc(&p.tm_q);
             tma_prefetch_desc(&p.tm_k);
             tma_prefetch_desc(&p.tm_v);
             if (Cfg::kInt8) tma_prefetch_desc(&p.tm_ks);
-            mbar_expect_tx(bar_q(), Cfg::kQBytes);
-            for (int t = 0; t < 2; ++t)
-                for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
-                    tma_load_4d(sQ + t * Cfg::kQTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
-                                hf * 128 / (Cfg::kInt8 ? 1 : 2), q0 + t * 128, h, b);
             bool ok = true;
-            int issued = 0;
-            for (int j = 0; j < n_kv && ok; ++j) {
-                for (int kv = 0; kv < 2 && ok; ++kv) {
-                    const int item = 2 * j + kv;
-                    const int slot = item % Cfg::kStages;
-                    const int use = item / Cfg::kStages;
-                    if (use > 0) ok = mbar_wait(bar_kv_empty(slot), (use - 1) & 1, kSiteKvEmpty, abort_flag);
-                    if (!ok) break;
-                    const uint32_t dst = sRing + slot * Cfg::kSlotBytes;
-                    if (kv) {
-                        mbar_expect_tx(bar_kv_full(slot), Cfg::kVTileBytes);
-                        for (int hf = 0; hf < Cfg::kVBoxes; ++hf)
-                            tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_v, bar_kv_full(slot),
-                                        hf * 64, j * Cfg::kBlockN, h, b);
-                    } else {
-                        mbar_expect_tx(bar_kv_full(slot), Cfg::kKTileBytes + Cfg::kKScaleBytes);
-                        for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
-                            tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_k, bar_kv_full(slot),
-                                        hf * 128 / (Cfg::kInt8 ? 1 : 2), j * Cfg::kBlockN, h, b);
-                        if (Cfg::kInt8)
-                            tma_load_2d(dst + Cfg::kKTileBytes, &p.tm_ks, bar_kv_full(slot),
-                                        j * Cfg::kBlockN, bh);
-                    }
-                    issued = item + 1;
+            int item = 0;  // running ring item (K_j, V_j, K_j+1, ...)
+            int au = 0;    // running active unit
+            auto load_item = [&](const Unit &x, int j, int kv) {
+                const int slot = item % Cfg::kStages, use = item / Cfg::kStages;
+                if (use > 0 && !(ok = mbar_wait(bar_kv_empty(slot), (use - 1) & 1, kSiteKvEmpty, abort_flag)))
+                    return;
+                const uint32_t dst = sRing + slot * Cfg::kSlotBytes;
+                if (kv) {
+                    mbar_expect_tx(bar_kv_full(slot), Cfg::kVTileBytes);
+                    for (int hf = 0; hf < Cfg::kVBoxes; ++hf)
+                        tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_v, bar_kv_full(slot), hf * 64,
+                                    j * Cfg::kBlockN, x.h, x.b);
+                } else {
+                    mbar_expect_tx(bar_kv_full(slot), Cfg::kKTileBytes + Cfg::kKScaleBytes);
+                    for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
+                        tma_load_4d(dst + hf * Cfg::kBoxBytes, &p.tm_k, bar_kv_full(slot),
+                                    hf * 128 / (Cfg::kInt8 ? 1 : 2), j * Cfg::kBlockN, x.h, x.b);
+                    if (Cfg::kInt8)
+                        tma_load_2d(dst + Cfg::kKTileBytes, &p.tm_ks, bar_kv_full(slot), j * Cfg::kBlockN, x.bh);
                 }
+                ++item;
+            };
+            for (int k = 0; k * G < n_units && ok; ++k) {
+                const int u = unit_of(k);
+                if (u >= n_units) continue;
+                const Unit x = unit_at(u);
+                if (x.n_kv == 0) continue;
+                // K_0, V_0 first: they only need free ring slots, while Q waits
+                // for the previous unit's last QK^T.
+                for (int it = 0; it < 2 && ok; ++it) load_item(x, 0, it);
+                if (!ok) break;
+                if (au > 0 && !(ok = mbar_wait(bar_q_empty, (au - 1) & 1, kSiteQ, abort_flag))) break;
+                mbar_expect_tx(bar_q(), Cfg::kQBytes);
+                for (int t = 0; t < 2; ++t)
+                    for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
+                        tma_load_4d(sQ + t * Cfg::kQTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
+                                    hf * 128 / (Cfg::kInt8 ? 1 : 2), x.q0 + t * 128, x.h, x.b);
+                for (int j = 1; j < x.n_kv && ok; ++j)
+                    for (int kv = 0; kv < 2 && ok; ++kv) load_item(x, j, kv);
+                ++au;
             }
-            // Drain: the last copy issued into each slot has landed before the
-            // CTA can exit (bounded; normally already complete).
-            mbar_wait(bar_q(), 0, kSiteQ, &no_abort);
-            for (int item = max(0, issued - Cfg::kStages); item < issued; ++item)
-                mbar_wait(bar_kv_full(item % Cfg::kStages), (item / Cfg::kStages) & 1, kSiteKvFull,
-                          &no_abort);
+            // Drain: the last Q and the last copy issued into each slot have
+            // landed before the CTA can exit (bounded; normally complete).
+            if (au > 0) mbar_wait(bar_q(), (au - 1) & 1, kSiteQ, &no_abort);
+            for (int i = max(0, item - Cfg::kStages); i < item; ++i)
+                mbar_wait(bar_kv_full(i % Cfg::kStages), (i / Cfg::kStages) & 1, kSiteKvFull, &no_abort);
         }
     } else if (warp == 9) {
         // ---------------------------------------------------------- MMA issuer
         regs_dec<Cfg::kRegsProducer>();
-        if (lane == 0 && n_kv > 0) {
+        if (lane == 0 && any_work) {
             constexpr uint32_t idesc_qk =
                 Cfg::kInt8 ? idesc_i8(128, 128) : idesc_f16(128, 128, kBF16, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, false, true);
-            bool ok = mbar_wait(bar_q(), 0, kSiteQ, abort_flag);
             auto issue_qk = [&](int i, int slot) {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
                 const uint32_t qa = sQ + i * Cfg::kQTileBytes;
@@ -295,54 +329,66 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                                 (acc || kk > 0) ? 1u : 0u);
                 }
             };
-            for (int j = 0; j < n_kv && ok; ++j) {
-                const int k_item = 2 * j, k_slot = k_item % Cfg::kStages;
-                const int v_item = 2 * j - 1, v_slot = (v_item + Cfg::kStages) % Cfg::kStages;
-                ok = mbar_wait(bar_kv_full(k_slot), (k_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag);
+            bool ok = true;
+            int ib = 0;  // ring item of this unit's K_0
+            int gt = 0;  // running tile (phase of s_full / p_full)
+            int au = 0;  // running active unit (phase of q_full / q_empty / o_full)
+            for (int k = 0; k * G < n_units && ok; ++k) {
+                const int u = unit_of(k);
+                if (u >= n_units) continue;
+                const Unit x = unit_at(u);
+                const int n_kv = x.n_kv;
+                if (n_kv == 0) continue;
+                if (!(ok = mbar_wait(bar_q(), au & 1, kSiteQ, abort_flag))) break;
+                for (int j = 0; j < n_kv && ok; ++j) {
+                    const int k_item = ib + 2 * j, k_slot = k_item % Cfg::kStages;
+                    const int v_item = ib + 2 * j - 1, v_slot = v_item % Cfg::kStages;
+                    ok = mbar_wait(bar_kv_full(k_slot), (k_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag);
+                    if (!ok) break;
+                    if (j > 0) {
+                        ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
+                             mbar_wait(bar_p(0), (gt + j - 1) & 1, kSiteP, abort_flag);
+                        if (!ok) break;
+                        if (au == 0) GAE_TRACE(kTrMmaP0, j - 1);
+                        tc_fence_after();
+                        issue_pv(0, v_slot, j - 1 > 0);
+                    }
+                    issue_qk(0, k_slot);
+                    umma_commit(bar_s(0));
+                    if (au == 0) GAE_TRACE(kTrMmaIssued0, j);
+                    if (j > 0) {
+                        ok = mbar_wait(bar_p(1), (gt + j - 1) & 1, kSiteP, abort_flag);
+                        if (!ok) break;
+                        if (au == 0) GAE_TRACE(kTrMmaP1, j - 1);
+                        tc_fence_after();
+                        issue_pv(1, v_slot, j - 1 > 0);
+                        umma_commit(bar_kv_empty(v_slot));
+                        // int8: both softmax groups have read K_{j-1}'s scales from its slot.
+                        if (Cfg::kInt8) mbar_arrive(bar_kv_empty((k_item - 2) % Cfg::kStages));
+                    }
+                    issue_qk(1, k_slot);
+                    umma_commit(bar_s(1));
+                    if (!Cfg::kInt8) umma_commit(bar_kv_empty(k_slot));
+                    if (j == n_kv - 1) umma_commit(bar_q_empty);  // Q may be reloaded after this
+                    if (au == 0) GAE_TRACE(kTrMmaIssued1, j);
+                }
                 if (!ok) break;
-                if (j > 0) {
-                    ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                         mbar_wait(bar_p(0), (j - 1) & 1, kSiteP, abort_flag);
-                    if (!ok) break;
-                    GAE_TRACE(kTrMmaP0, j - 1);
-                    tc_fence_after();
-                    issue_pv(0, v_slot, j - 1 > 0);
-                }
-                issue_qk(0, k_slot);
-                umma_commit(bar_s(0));
-                GAE_TRACE(kTrMmaIssued0, j);
-                if (j > 0) {
-                    ok = mbar_wait(bar_p(1), (j - 1) & 1, kSiteP, abort_flag);
-                    if (!ok) break;
-                    GAE_TRACE(kTrMmaP1, j - 1);
-                    tc_fence_after();
-                    issue_pv(1, v_slot, j - 1 > 0);
-                    umma_commit(bar_kv_empty(v_slot));
-                    // int8: both softmax groups have read K_{j-1}'s scales from its slot.
-                    if (Cfg::kInt8) mbar_arrive(bar_kv_empty(((2 * j - 2) % Cfg::kStages)));
-                }
-                issue_qk(1, k_slot);
-                umma_commit(bar_s(1));
-                if (!Cfg::kInt8) umma_commit(bar_kv_empty(k_slot));
-                GAE_TRACE(kTrMmaIssued1, j);
-            }
-            if (ok) {
-                const int v_item = 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
+                const int v_item = ib + 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
                 ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                     mbar_wait(bar_p(0), (n_kv - 1) & 1, kSiteP, abort_flag);
-                if (ok) {
-                    tc_fence_after();
-                    issue_pv(0, v_slot, n_kv > 1);
-                    umma_commit(bar_o(0));
-                    ok = mbar_wait(bar_p(1), (n_kv - 1) & 1, kSiteP, abort_flag);
-                }
-                if (ok) {
-                    tc_fence_after();
-                    issue_pv(1, v_slot, n_kv > 1);
-                    umma_commit(bar_o(1));
-                    umma_commit(bar_kv_empty(v_slot));
-                    if (Cfg::kInt8) mbar_arrive(bar_kv_empty((2 * n_kv - 2) % Cfg::kStages));
-                }
+                     mbar_wait(bar_p(0), (gt + n_kv - 1) & 1, kSiteP, abort_flag);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(0, v_slot, n_kv > 1);
+                umma_commit(bar_o(0));
+                if (!(ok = mbar_wait(bar_p(1), (gt + n_kv - 1) & 1, kSiteP, abort_flag))) break;
+                tc_fence_after();
+                issue_pv(1, v_slot, n_kv > 1);
+                umma_commit(bar_o(1));
+                umma_commit(bar_kv_empty(v_slot));
+                if (Cfg::kInt8) mbar_arrive(bar_kv_empty((v_item - 1) % Cfg::kStages));
+                ib += 2 * n_kv;
+                gt += n_kv;
+                ++au;
             }
             // Drain: every MMA this thread issued has completed before TMEM is
             // freed (bounded, and not cut short by the abort flag).
@@ -355,11 +401,18 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         const int grp = warp >> 2;       // Q tile 0 or 1
         const int wq = warp & 3;         // TMEM lane quarter
         const int row = wq * 32 + lane;  // row within the Q tile
-        const int q_local = q0 + grp * 128 + row;
-        const int64_t q_abs = p.q_offset + q_local;
         const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
         const uint32_t tS = tmem + lane_off + (grp ? Cfg::kColS1 : Cfg::kColS0);
         const uint32_t tO = tmem + lane_off + (grp ? Cfg::kColO1 : Cfg::kColO0);
+        bool ok = true;
+        int ib = 0, gt = 0, au = 0;  // same running counters as the MMA issuer
+        for (int k = 0; k * G < n_units && ok; ++k) {
+                const int u = unit_of(k);
+                if (u >= n_units) continue;
+        const Unit x = unit_at(u);
+        const int n_kv = x.n_kv, b = x.b, h = x.h, bh = x.bh;
+        const int q_local = x.q0 + grp * 128 + row;
+        const int64_t q_abs = p.q_offset + q_local;
         // Factor that takes a raw score to the log2 domain: scale*log2(e), times
         // the query row's dequantisation scale in int8 mode.
         float sl2 = p.scale_log2;
@@ -372,11 +425,10 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
 
         float m_run = -INFINITY;  // exponent base, log2 domain (scaled)
         float l_run = 0.f;
-        bool ok = true;
         for (int j = 0; j < n_kv; ++j) {
-            ok = mbar_wait(bar_s(grp), j & 1, kSiteS, abort_flag);
+            ok = mbar_wait(bar_s(grp), (gt + j) & 1, kSiteS, abort_flag);
             if (!ok) break;
-            if (row == 0) GAE_TRACE(kTrSWait0 + grp, j);
+            if (row == 0 && au == 0) GAE_TRACE(kTrSWait0 + grp, j);
             tc_fence_after();
             float s[128];
             {
@@ -390,8 +442,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     // Exact int32 logits times the keys' dequantisation scales.  The
                     // scales arrived with K_j; its slot is released only after both
                     // softmax groups finished tile j.
-                    const int slot = (2 * j) % Cfg::kStages;
-                    if (!mbar_wait(bar_kv_full(slot), ((2 * j) / Cfg::kStages) & 1, kSiteKvFull,
+                    const int slot = (ib + 2 * j) % Cfg::kStages;
+                    if (!mbar_wait(bar_kv_full(slot), ((ib + 2 * j) / Cfg::kStages) & 1, kSiteKvFull,
                                    abort_flag)) {
                         ok = false;
                         break;
@@ -497,13 +549,14 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(bar_p(grp));
-            if (row == 0) GAE_TRACE(kTrPDone0 + grp, j);
+            if (row == 0 && au == 0) GAE_TRACE(kTrPDone0 + grp, j);
         }
+        if (!ok) break;
 
         // Epilogue: O_i / l -> global; log-sum-exp.
         const bool row_valid = q_local < p.Nq;
         const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
-        if (n_kv > 0 && ok) ok = mbar_wait(bar_o(grp), 0, kSiteO, abort_flag);
+        if (n_kv > 0 && ok) ok = mbar_wait(bar_o(grp), au & 1, kSiteO, abort_flag);
         if (n_kv > 0 && ok) {
             tc_fence_after();
             char *orow = reinterpret_cast<char *>(p.o) +
@@ -537,11 +590,17 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             if (l_run > 0.f) lse = (m_run + __log2f(l_run)) * 0.69314718055994531f;
             p.lse[(int64_t)bh * p.Nq + q_local] = lse;
         }
+        if (n_kv > 0) {
+            ib += 2 * n_kv;
+            gt += n_kv;
+            ++au;
+        }
+        }  // units
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 9 && n_kv > 0) {
+    if (warp == 9 && any_work) {
         __syncwarp();
         tc_fence_after();
         tmem_dealloc(tmem, Cfg::kTmemCols);
