@@ -10,7 +10,8 @@
 //     X [M, K] and W [N, K] bf16, both K-major, arrive by TMA (128-byte
 //     swizzle) into a 4-stage shared-memory ring; one thread issues
 //     128x256x16 MMAs into one of two TMEM accumulators (2 x 256 columns);
-//     four epilogue warps drain the other accumulator (thread = output row)
+//     eight epilogue warps drain the other accumulator (thread = output row,
+//     two warps per row quarter, one per column half)
 //     and fuse bias, tanh-GELU or the residual add, writing bf16.
 //   * layernorm_kernel: one warp per row, 16-byte vector loads, fp32
 //     statistics (population variance, eps inside the square root, as
@@ -44,7 +45,7 @@ struct LinearCfg {
     // full[S], empty[S], acc_full[2], acc_empty[2], done
     static constexpr int kNumBars = 2 * kStages + 5;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
-    static constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+    static constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 };
 
 enum LinearWaitSite : unsigned {
@@ -62,7 +63,7 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.f + t);
 }
 
-__global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ LinearParams p) {
+__global__ void __launch_bounds__(320, 1) linear_kernel(const __grid_constant__ LinearParams p) {
     using Cfg = LinearCfg;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -89,7 +90,7 @@ __global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ 
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(bar_acc_full(b), 1);
-            mbar_init(bar_acc_empty(b), 128);
+            mbar_init(bar_acc_empty(b), 256);
         }
         mbar_init(bar_done, 1);
         *abort_flag = 0;
@@ -159,8 +160,10 @@ __global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ 
             mbar_wait(bar_done, 0, kSiteLinDone, &no_abort);
         }
     } else {
-        // Epilogue warps 2-5: TMEM lane quarter = warp % 4, thread = row.
+        // Epilogue warps 2-9: TMEM lane quarter = warp % 4 (thread = row); warps
+        // 2-5 take columns [0, 128) of the tile, warps 6-9 columns [128, 256).
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         int local = 0;
@@ -174,13 +177,19 @@ __global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ 
             __nv_bfloat16 *yrow = p.y + (int64_t)m * p.ldy + n0;
             const __nv_bfloat16 *rrow = (p.epi == kEpiBiasResidual) ? p.res + (int64_t)m * p.ldr + n0 : nullptr;
 #pragma unroll 1
-            for (int c = 0; c < Cfg::BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(tmem + lane_off + b * Cfg::BN + c * 32, r);
+            for (int cc = 0; cc < 2; ++cc) {
+                // 64 columns per TMEM wait.
+                uint32_t r[2][32];
+                const int c0 = half * 4 + cc * 2;
+                tmem_ld32(tmem + lane_off + b * Cfg::BN + c0 * 32, r[0]);
+                tmem_ld32(tmem + lane_off + b * Cfg::BN + c0 * 32 + 32, r[1]);
                 tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                const int c = c0 + i;
                 float v[32];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
+                for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[i][e]);
                 if (p.bias) {
                     const float4 *bp = reinterpret_cast<const float4 *>(p.bias + n0 + c * 32);
 #pragma unroll
@@ -211,6 +220,7 @@ __global__ void __launch_bounds__(192, 1) linear_kernel(const __grid_constant__ 
                     for (int q = 0; q < 4; ++q)
                         dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
                                             pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+                }
                 }
             }
             tc_fence_before();
