@@ -398,6 +398,10 @@ gae_status make_map_kmajor(CUtensorMap *m, const void *ptr, int64_t rows, int64_
 }
 
 
+#ifndef GAE_LINEAR_2SM
+#define GAE_LINEAR_2SM 1
+#endif
+
 gae_status launch_linear(const void *x, int64_t ldx, const void *w, const float *bias, const void *res,
                          int64_t ldr, void *y, int64_t ldy, int64_t M, int64_t N, int64_t K, int epi,
                          cudaStream_t st) {
@@ -427,10 +431,21 @@ gae_status launch_linear(const void *x, int64_t ldx, const void *w, const float 
     p.epi = epi;
     p.tiles_m = (int)((M + Cfg::BM - 1) / Cfg::BM);
     p.tiles_n = (int)(N / Cfg::BN);
+#if GAE_LINEAR_2SM
+    // CTA pairs on 256 x 256 tiles (the kernel derives its own tile counts).
+    if ((s = make_map_kmajor(&p.tm_a, x, M, K, ldx, 128)) != GAE_OK) return s;
+    if ((s = make_map_kmajor(&p.tm_b, w, N, K, K, 128)) != GAE_OK) return s;
+    using Cfg2 = gae::Linear2Cfg;
+    const int tiles2 = (int)((M + Cfg2::BM - 1) / Cfg2::BM) * (int)(N / Cfg2::BN);
+    const int pairs = tiles2 < num_sms() / 2 ? tiles2 : num_sms() / 2;
+    if ((s = set_smem(gae::linear2_kernel, Cfg2::kSmemBytes)) != GAE_OK) return s;
+    gae::linear2_kernel<<<2 * pairs, Cfg2::kThreads, Cfg2::kSmemBytes, st>>>(p);
+#else
     const int tiles = p.tiles_m * p.tiles_n;
     if ((s = set_smem(gae::linear_kernel, Cfg::kSmemBytes)) != GAE_OK) return s;
     const int grid = tiles < num_sms() ? tiles : num_sms();
     gae::linear_kernel<<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(p);
+#endif
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }

@@ -236,6 +236,205 @@ __global__ void __launch_bounds__(320, 1) linear_kernel(const __grid_constant__ 
     }
 }
 
+
+// ------------------------------------------------------- 2-SM linear layer
+// The same GEMM with the epilogues above on CTA pairs (a cluster of 2): the
+// pair computes a 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256).
+// Each CTA holds its own 128 rows of X and its own 128 rows (one N half) of
+// W per stage, so each SM streams half as many weight bytes per FLOP as the
+// one-SM kernel and a stage is 32 KB, leaving room for 6 stages.  The
+// leader CTA (rank 0) owns the pipeline: both CTAs' TMA copies complete on
+// its "full" barriers, its one thread issues the MMAs, and its commits reach
+// the "empty" and "accumulator full" barriers of both CTAs.  Each CTA's
+// TMEM holds its 128 rows of the two 256-column accumulators; each CTA's
+// eight epilogue warps drain its rows and arrive on the leader's
+// "accumulator empty" barrier.
+struct Linear2Cfg {
+    static constexpr int BM = 256, BN = 256, BK = 64;  // pair tile
+    static constexpr int kStages = 6;
+    static constexpr int kABytes = 128 * BK * 2;        // this CTA's 128 rows of X
+    static constexpr int kBBytes = 128 * BK * 2;        // this CTA's N half of W
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kBarOffset = kStages * kStageBytes;
+    // full[S], empty[S], acc_full[2], acc_empty[2], done
+    static constexpr int kNumBars = 2 * kStages + 5;
+    static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+    static constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
+    linear2_kernel(const __grid_constant__ LinearParams p) {
+    using Cfg = Linear2Cfg;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    const uint32_t base = (raw_addr + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base - raw_addr);
+    const uint32_t sBar = base + Cfg::kBarOffset;
+    auto bar_full = [&](int s) { return sBar + 8u * s; };
+    auto bar_empty = [&](int s) { return sBar + 8u * (Cfg::kStages + s); };
+    auto bar_acc_full = [&](int b) { return sBar + 8u * (2 * Cfg::kStages + b); };
+    auto bar_acc_empty = [&](int b) { return sBar + 8u * (2 * Cfg::kStages + 2 + b); };
+    const uint32_t bar_done = sBar + 8u * (2 * Cfg::kStages + 4);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kBarOffset + Cfg::kNumBars * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int no_abort = 0;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
+    const int tiles_m = (p.M + Cfg::BM - 1) / Cfg::BM, tiles_n = p.N / Cfg::BN;
+    const int n_tiles = tiles_m * tiles_n;
+    const int kb_count = p.K / Cfg::BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::kStages; ++s) {
+            mbar_init(bar_full(s), 1);
+            mbar_init(bar_empty(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bar_acc_full(b), 1);
+            mbar_init(bar_acc_empty(b), 2 * 256);  // epilogue threads of both CTAs
+        }
+        mbar_init(bar_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers of both CTAs initialised before any remote use
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            tma_prefetch_desc(&p.tm_a);
+            tma_prefetch_desc(&p.tm_b);
+            int it = 0;
+            bool ok = true;
+            for (int t = pair; t < n_tiles && ok; t += n_pairs) {
+                const int m0 = (t / tiles_n) * Cfg::BM + (int)rank * 128;
+                const int n0 = (t % tiles_n) * Cfg::BN + (int)rank * 128;
+                for (int kb = 0; kb < kb_count; ++kb, ++it) {
+                    const int s = it % Cfg::kStages, use = it / Cfg::kStages;
+                    if (use > 0 && !(ok = mbar_wait(bar_empty(s), (use - 1) & 1, kSiteLinEmpty, abort_flag)))
+                        break;
+                    if (leader) mbar_expect_tx(bar_full(s), 2 * Cfg::kStageBytes);
+                    const uint32_t full0 = mapa_shared(bar_full(s), 0);
+                    const uint32_t dst = base + s * Cfg::kStageBytes;
+                    tma_load_2d_pair(dst, &p.tm_a, full0, kb * Cfg::BK, m0);
+                    tma_load_2d_pair(dst + Cfg::kABytes, &p.tm_b, full0, kb * Cfg::BK, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            constexpr uint32_t idesc = idesc_f16(Cfg::BM, Cfg::BN, true, false, false);
+            int it = 0, local = 0;
+            bool ok = true;
+            for (int t = pair; t < n_tiles && ok; t += n_pairs, ++local) {
+                const int b = local & 1, use = local >> 1;
+                if (use > 0 && !(ok = mbar_wait(bar_acc_empty(b), (use - 1) & 1, kSiteLinAccEmpty, abort_flag)))
+                    break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * Cfg::BN;
+                for (int kb = 0; kb < kb_count; ++kb, ++it) {
+                    const int s = it % Cfg::kStages;
+                    if (!(ok = mbar_wait(bar_full(s), (it / Cfg::kStages) & 1, kSiteLinFull, abort_flag))) break;
+                    tc_fence_after();
+                    const uint32_t sa = base + s * Cfg::kStageBytes, sb = sa + Cfg::kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < Cfg::BK / 16; ++kk)
+                        umma_f16_ss_pair(acc, smem_desc_sw128(sa + kk * 32, 16, 1024),
+                                         smem_desc_sw128(sb + kk * 32, 16, 1024), idesc,
+                                         (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_commit_pair_both(bar_empty(s));
+                }
+                if (ok) umma_commit_pair_both(bar_acc_full(b));
+            }
+            // Drain: all issued MMAs complete before TMEM is released.
+            umma_commit_pair(bar_done);
+            mbar_wait(bar_done, 0, kSiteLinDone, &no_abort);
+        }
+    } else {
+        // Epilogue warps 2-9, as in linear_kernel, on this CTA's 128 rows.
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        int local = 0;
+        for (int t = pair; t < n_tiles; t += n_pairs, ++local) {
+            const int b = local & 1, use = local >> 1;
+            if (!mbar_wait(bar_acc_full(b), use & 1, kSiteLinAccFull, abort_flag)) break;
+            tc_fence_after();
+            const int m = (t / tiles_n) * Cfg::BM + (int)rank * 128 + row;
+            const int n0 = (t % tiles_n) * Cfg::BN;
+            const bool valid = m < p.M;
+            __nv_bfloat16 *yrow = p.y + (int64_t)m * p.ldy + n0;
+            const __nv_bfloat16 *rrow = (p.epi == kEpiBiasResidual) ? p.res + (int64_t)m * p.ldr + n0 : nullptr;
+#pragma unroll 1
+            for (int cc = 0; cc < 2; ++cc) {
+                uint32_t r[2][32];
+                const int c0 = half * 4 + cc * 2;
+                tmem_ld32(tmem + lane_off + b * Cfg::BN + c0 * 32, r[0]);
+                tmem_ld32(tmem + lane_off + b * Cfg::BN + c0 * 32 + 32, r[1]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int c = c0 + i;
+                    float v[32];
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[i][e]);
+                    if (p.bias) {
+                        const float4 *bp = reinterpret_cast<const float4 *>(p.bias + n0 + c * 32);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            const float4 bb = __ldg(bp + q);
+                            v[4 * q] += bb.x; v[4 * q + 1] += bb.y; v[4 * q + 2] += bb.z; v[4 * q + 3] += bb.w;
+                        }
+                    }
+                    if (p.epi == kEpiBiasGelu) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] = gelu_tanh(v[e]);
+                    } else if (p.epi == kEpiBiasResidual && valid) {
+                        const uint4 *rp = reinterpret_cast<const uint4 *>(rrow + c * 32);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            const uint4 rv = rp[q];
+                            const uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                v[8 * q + 2 * u] += __uint_as_float(w4[u] << 16);
+                                v[8 * q + 2 * u + 1] += __uint_as_float(w4[u] & 0xffff0000u);
+                            }
+                        }
+                    }
+                    if (valid) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(yrow + c * 32);
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            dst[q] = make_uint4(pack_bf16x2(v[8 * q], v[8 * q + 1]), pack_bf16x2(v[8 * q + 2], v[8 * q + 3]),
+                                                pack_bf16x2(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2(v[8 * q + 6], v[8 * q + 7]));
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_remote(mapa_shared(bar_acc_empty(b), 0));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the leader's MMAs no longer read either CTA's smem or TMEM
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
 // ------------------------------------------------------------- LayerNorm
 // One warp per row.  s = x (+ res, rounded to bf16 and written to sum_out);
 // y = (s - mean) / sqrt(var + eps) * gamma + beta with the population
