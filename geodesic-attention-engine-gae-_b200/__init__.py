@@ -104,6 +104,7 @@ def lib():
     L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
     L.gae_linear_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
+    L.gae_debug_wait_timeout.argtypes = [C.c_uint64, vp]
     _lib = L
     return L
 

@@ -592,6 +592,30 @@ gae_status gae_device_status(int reset) {
     return GAE_OK;
 }
 
+namespace gae {
+// One thread waits, with a bounded wait, on an mbarrier that nothing arrives
+// on: the wait gives up after timeout_ns, records `site` and returns; no
+// asynchronous copy or MMA is in flight, so the kernel exits cleanly.
+__global__ void wait_timeout_probe_kernel(uint64_t timeout_ns, unsigned site) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mbar_wait_for(smem_u32(&bar), 0, site, &abort_flag, timeout_ns);
+}
+}  // namespace gae
+
+extern "C" gae_status gae_debug_wait_timeout(uint64_t timeout_ns, void *stream) {
+    if (timeout_ns > 1000000000ull) return fail(GAE_ERR_INVALID_ARG, "timeout above 1 s");
+    gae::wait_timeout_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(timeout_ns, 0x901u);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
 gae_status gae_debug_attn_trace(void *buf, int cta) {
 #ifndef GAE_ATTN_TRACE
     (void)buf; (void)cta;

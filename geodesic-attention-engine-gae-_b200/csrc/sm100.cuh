@@ -70,23 +70,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// records `site`) if it does not complete within GAE_WAIT_TIMEOUT_NS, or if
-// another thread of the CTA already gave up (abort flag in shared memory).
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned site,
-                                          volatile int *abort_flag) {
+// records `site`) if it does not complete within timeout_ns, or if another
+// thread of the CTA already gave up (abort flag in shared memory).
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, unsigned site,
+                                              volatile int *abort_flag, uint64_t timeout_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     uint64_t t0 = globaltimer();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (*abort_flag) return false;
-            if (globaltimer() - t0 > GAE_WAIT_TIMEOUT_NS) {
+            if (globaltimer() - t0 > timeout_ns) {
                 *abort_flag = 1;
                 record_error(site);
                 return false;
             }
         }
     }
+}
+
+// The library's waits: bounded by GAE_WAIT_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned site,
+                                          volatile int *abort_flag) {
+    return mbar_wait_for(bar, parity, site, abort_flag, GAE_WAIT_TIMEOUT_NS);
 }
 
 // -------------------------------------------------------------------- TMA

@@ -21,6 +21,11 @@ while it sends that block to rank r+1 and receives the next one from rank r-1
 the compute stream).  K and V travel as one packed buffer; remote blocks land
 in this GPU's own memory before any kernel reads them.
 
+Failure handling: a rank that dies, leaves, or never joins a step makes the
+other ranks' exchange fail (an error from the backend or the process group's
+timeout); the driver raises GAEError(GAE_ERR_COMM) naming the step.  The
+timeout is the process group's (init_process_group(timeout=...)).
+
 `attend` and `merge` are injectable so that the host logic can be exercised on
 CPU ranks (gloo) in tests; the product path uses the CUDA kernels and fails
 loudly without them.
@@ -42,6 +47,22 @@ def _default_attend(q, k, v, causal, q_offset, kv_offset, scale):
 def _default_merge(o_acc, lse_acc, o_part, lse_part):
     from . import lse_merge_
     lse_merge_(o_acc, lse_acc, o_part, lse_part)
+
+
+def _comm_error(what, exc):
+    from . import GAEError
+    return GAEError(5, f"ring attention: {what} failed: {exc}")
+
+
+def _exchange(ops, what):
+    """Runs a batch of point-to-point operations and waits for it.  A peer
+    that died, left, or stayed away past the process group's timeout surfaces
+    here as GAEError(GAE_ERR_COMM) instead of an opaque backend error."""
+    try:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+    except Exception as e:  # backend errors carry no common type
+        raise _comm_error(what, e) from e
 
 
 def zigzag_owner(chunk: int, P: int) -> int:
@@ -95,8 +116,7 @@ def _redeal(x, rank, P, group, to_zigzag: bool):
     for dst_view, src_view in local:
         dst_view.copy_(src_view)
     if ops:
-        for w in dist.batch_isend_irecv(ops):
-            w.wait()
+        _exchange(ops, "re-dealing the shards")
     for dst_view, buf in recv:
         dst_view.copy_(buf)
     return out
@@ -143,7 +163,10 @@ def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "
         if t < P - 1:
             ops = [dist.P2POp(dist.isend, kv, (r + 1) % P, group),
                    dist.P2POp(dist.irecv, kv_next, (r - 1) % P, group)]
-            reqs = dist.batch_isend_irecv(ops)
+            try:
+                reqs = dist.batch_isend_irecv(ops)
+            except Exception as e:
+                raise _comm_error(f"posting the K/V exchange of step {t}", e) from e
         for qi, (qc, qo, ql) in enumerate(chunks_of(r)):
             for kc, ko, kl in chunks_of(src):
                 if causal and kc > qc:
@@ -155,8 +178,11 @@ def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "
                     acc[qi] = (o_p.float().contiguous(), l_p.contiguous())
                 else:
                     merge(acc[qi][0], acc[qi][1], o_p.contiguous(), l_p.contiguous())
-        for w in reqs:
-            w.wait()
+        try:
+            for w in reqs:
+                w.wait()
+        except Exception as e:
+            raise _comm_error(f"the K/V exchange of step {t}", e) from e
         if t < P - 1:
             kv, kv_next = kv_next, kv
 

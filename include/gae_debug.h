@@ -28,6 +28,13 @@ extern "C" {
  * from the heaviest query block (x = 0 is the last 256 query rows). */
 GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
 
+/* Exercises the library's bounded device-side wait: launches one thread that
+ * waits on an mbarrier nothing will complete, with a limit of timeout_ns
+ * (at most 1 s).  The wait gives up, records site 0x901 and the kernel exits
+ * normally; gae_device_status() then reports GAE_ERR_TIMEOUT and the CUDA
+ * context stays usable.  For testing failure detection without a GPU fault. */
+GAE_API gae_status gae_debug_wait_timeout(uint64_t timeout_ns, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
