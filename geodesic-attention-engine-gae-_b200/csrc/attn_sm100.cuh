@@ -51,6 +51,7 @@ struct AttnParams {
     int64_t o_sb, o_sh, o_ss;  // element strides of O
     int B, H, Nq, Nkv;
     int n_qpairs;
+    int head_major;  // unit order: 1 = all query blocks of a head in a row, 0 = heaviest first
     int causal;
     float scale_log2;  // scale * log2(e)
     int64_t q_offset, kv_offset;
@@ -188,8 +189,10 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     struct Unit { int q0, b, h, bh, n_kv; };
     auto unit_at = [&](int u) {
         Unit x;
-        const int qpair = p.n_qpairs - 1 - u / BH;
-        x.bh = u % BH;
+        // head-major keeps the K/V of a head in L2 while its query blocks run
+        // side by side; heaviest first balances a persistent grid.
+        const int qpair = p.n_qpairs - 1 - (p.head_major ? u % p.n_qpairs : u / BH);
+        x.bh = p.head_major ? u / p.n_qpairs : u % BH;
         x.b = x.bh / p.H;
         x.h = x.bh % p.H;
         x.q0 = qpair * 256;

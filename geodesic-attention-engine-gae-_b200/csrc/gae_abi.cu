@@ -185,7 +185,9 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     // gain most from keeping TMEM, barriers and the K/V stream alive, measured
     // +20%).  head_dim 128: one CTA per unit, balanced by the hardware's block
     // scheduler (equal or better under the power cap, measured).
-    dim3 grid((unsigned)((D == 64 && units > num_sms()) ? num_sms() : units));
+    const bool persistent = D == 64 && units > num_sms();
+    p.head_major = persistent ? 0 : 1;
+    dim3 grid((unsigned)(persistent ? num_sms() : units));
 
     if (D == 128) {
         if (bf16) s = launch_tc<128, gae::kModeBF16>(p, grid, st);
@@ -224,6 +226,7 @@ gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st) {
     p.causal = a->causal ? 1 : 0;
     p.scale_log2 = a->scale * 1.4426950408889634f;
     const int64_t units = (int64_t)p.n_qpairs * BH;
+    p.head_major = 1;
     dim3 grid((unsigned)units);  // one CTA per unit (measured faster than persistent for int8)
     return launch_tc<128, gae::kModeInt8>(p, grid, st);
 }
