@@ -11,6 +11,8 @@ Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
   ring           config 5, causal: one sequence of N=1,048,576 (H=8, head_dim=128)
                  sharded over the N GPUs (contiguous N/P shards, ring attention with
                  zig-zag balance, K/V rotated by NCCL send/recv; strong scaling)
+  ulysses        config 5 like `ring`, but sequence parallel by head/sequence
+                 all-to-all (each rank attends the whole sequence for H/P heads)
   int8           config 3: B=1, H=32, N=16384, head_dim=128, non-causal; Q, K
                  quantised per row to int8 (fp32 scales), V bf16; QK^T on the int8
                  tensor cores (int32 accumulation), P*V in bf16.  Ops counted as
@@ -55,6 +57,8 @@ WORKLOADS = {
     "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
     "mha64": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-attention-d64"),
     "ring": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M", ring=True),
+    "ulysses": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ulysses-1M", ring=True,
+                    sp="ulysses"),
     "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
     "gpt2": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-gpt2-small-12L", gpt2=True,
                  layers=12, d_model=768, d_ff=3072),
@@ -350,8 +354,14 @@ def main():
         out = torch.empty_like(q)
         flops = attn_flops(B, H, N, N, D, causal) / world  # per rank share of the job
 
-        def run_step(q, k, v):
-            out.copy_(ring.ring_attention(q, k, v, causal=causal))
+        if w.get("sp") == "ulysses":
+            from gae_b200 import ulysses
+
+            def run_step(q, k, v):
+                out.copy_(ulysses.ulysses_attention(q, k, v, causal=causal))
+        else:
+            def run_step(q, k, v):
+                out.copy_(ring.ring_attention(q, k, v, causal=causal))
     else:
         q, k, v = make_inputs(torch, w, dev, 1000 + rank)
         out = torch.empty_like(q)
@@ -382,7 +392,10 @@ def main():
 
     # kernels of this library per step: the ring runs 3 block pairs + 1 merge at
     # P=1 and 2 pairs + 2 merges per further step (zig-zag balance).
-    launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
+    if is_ring and w.get("sp") == "ulysses":
+        launches_per_step = 1
+    else:
+        launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
 
     # ---- end to end through the public API with host buffers ---------------
     def flat(t):
@@ -480,7 +493,7 @@ def main():
         "data": "synthetic",
         "config": {"workload": w["cfg"], "B": B, "H": H, "seq_len": N, "head_dim": D,
                    "causal": causal, "global_batch": B if is_ring else B * world,
-                   "parallelism": (f"ring-sp{world}" if is_ring else f"dp{world}") if world > 1 else "single",
+                   "parallelism": ((f"{w.get('sp', 'ring')}-sp{world}") if is_ring else f"dp{world}") if world > 1 else "single",
                    "l2": "inputs larger than L2 (no flush)"},
         "e2e": {"value": e2e_value, "unit": "TFLOPS", "h2d_bytes_per_step": bytes_in,
                 "d2h_bytes_per_step": bytes_out, "ms_per_step": e2e_ms,
