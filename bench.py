@@ -48,6 +48,8 @@ import subprocess
 import sys
 import time
 
+import numpy as np
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
@@ -62,6 +64,10 @@ WORKLOADS = {
     "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
     "gpt2": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-gpt2-small-12L", gpt2=True,
                  layers=12, d_model=768, d_ff=3072),
+    # the reference's fused symphony layer (waller_fused_layer.cu:64-247) at its
+    # benchmark's largest single-launch length with HEAD_DIM 64 (:17, :407)
+    "symphony": dict(B=1, H=1, N=131072, D=64, causal=True, cfg="symphony-layer-131072-d64",
+                     sym=True, metric="fused symphony layer TFLOPS (d=64, int8 K/V)"),
 }
 METRIC = "fused-attention TFLOPS (bf16 d=128)"
 
@@ -156,6 +162,26 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def symphony_flops(N, D):
+    """Causal attention (4*D per query-key pair, as for every workload here),
+    the MLP (2 x 2*D*4D per token) and the two RMSNorms (4*D per token each)."""
+    return attn_flops(1, 1, N, N, D, True) + 16.0 * N * D * D + 8.0 * N * D
+
+
+def symphony_arrays(N, D, seed):
+    """The reference benchmark's input distribution (waller_fused_layer.cu:
+    265-283): inputs uniform in [-0.5, 0.5), K/V uniform int8, weights uniform
+    in [-0.05, 0.05), unit norm weights; seeded numpy instead of rand()."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    return dict(x=(rng.integers(0, 1000, (N, D)) / 1000.0 - 0.5).astype(np.float32),
+                k=rng.integers(-128, 128, (N, D)).astype(np.int8),
+                v=rng.integers(-128, 128, (N, D)).astype(np.int8),
+                w_up=(rng.integers(0, 1000, (D, 4 * D)) / 10000.0 - 0.05).astype(np.float32),
+                w_down=(rng.integers(0, 1000, (4 * D, D)) / 10000.0 - 0.05).astype(np.float32),
+                n1=np.ones(D, np.float32), n2=np.ones(D, np.float32))
+
+
 def make_inputs(torch, w, device, seed):
     g = torch.Generator(device="cpu").manual_seed(seed)
     shape = (w["B"], w["H"], w["N"], w["D"])
@@ -199,6 +225,18 @@ def cpu_sample(w, slices=8, rows_cap=None):
         flops = 4.0 * D * n_rows * N * slices
         return (flops / dt / 1e12, dt, f"{slices} head(s) x {n_rows} query rows, full key range each",
                 oracle.num_threads())
+    if w.get("sym"):
+        # the first `rows_cap` tokens: a causal prefix is a complete layer of its own
+        n = N if rows_cap is None else min(N, rows_cap)
+        a = symphony_arrays(n, D, 1234)
+        tf = (1.0 / (math.sqrt(D) * 127.0 * 127.0), 1.0, 1.0, 1.0, 1e-6, 1.0, 1.0)
+        oracle.lib()
+        t0 = time.perf_counter()
+        oracle.symphony_layer(a["x"], a["k"], a["v"], a["w_up"], a["w_down"], a["n1"], a["n2"], tf, 0)
+        dt = time.perf_counter() - t0
+        return (symphony_flops(n, D) / dt / 1e12, dt,
+                f"symphony layer over the first {n} tokens (causal prefix, fp32 oracle)",
+                oracle.num_threads())
     q, k, v = (rng.standard_normal((1, slices, N, D)).astype(np.float32) for _ in range(3))
     n_rows = N if rows_cap is None else min(N, rows_cap)
     rows = None if n_rows == N else np.linspace(0, N - 1, n_rows).round().astype(np.int64)
@@ -232,6 +270,21 @@ def run_reference(args, w):
             v, s, desc, threads = cpu_sample(w)
             vals.append(v); secs.append(s)
         return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
+    if w.get("sym") and args.reference_kernel:
+        return run_reference_kernel(args, w)
+    if w.get("sym"):
+        # cost grows with the square of the prefix length: calibrate at 4096
+        _, s_cal, _, _ = cpu_sample(w, rows_cap=4096)
+        budget = 120.0 / (args.steps + args.warmup)
+        n = int(min(w["N"], 4096 * math.sqrt(budget / max(s_cal, 1e-6))))
+        n = max(1024, n // 256 * 256)
+        for _ in range(args.warmup):
+            cpu_sample(w, rows_cap=n)
+        vals, secs = [], []
+        for _ in range(args.steps):
+            v, s, desc, threads = cpu_sample(w, rows_cap=n)
+            vals.append(v); secs.append(s)
+        return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
     # Calibrate: seconds per row of one slice (full key range).
     _, s_cal, _, _ = cpu_sample(w, slices=1, rows_cap=256)
     per_row = s_cal / 256
@@ -248,9 +301,51 @@ def run_reference(args, w):
     return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
 
 
+def run_reference_kernel(args, w):
+    """The reference's own symphony CUDA kernel (built from its source into
+    oracle/_ref by the oracle's Makefile) on this GPU, same workload and input
+    distribution; CUDA-event timed.  A comparison point, not the CPU arm."""
+    import torch
+    from oracle import oracle
+    L = oracle.ref_symphony()
+    if L is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          "reference symphony kernel not built (oracle/_ref missing)"}))
+        return 0
+    N, D = w["N"], w["D"]
+    a = {n_: torch.from_numpy(v_).cuda() for n_, v_ in symphony_arrays(N, D, 1000).items()}
+    out = torch.empty_like(a["x"])
+    tf = np.asarray((1.0 / (math.sqrt(D) * 127.0 * 127.0), 1.0, 1.0, 1.0, 1e-6, 1.0, 1.0), np.float32)
+    st = torch.cuda.current_stream()
+
+    def launch():
+        rc = L.ref_symphony_fwd(a["k"].data_ptr(), a["v"].data_ptr(), a["w_up"].data_ptr(),
+                                a["w_down"].data_ptr(), a["n1"].data_ptr(), a["n2"].data_ptr(),
+                                a["x"].data_ptr(), out.data_ptr(), N, tf, 0, st.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"reference kernel launch failed: {rc}")
+
+    launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, min(args.steps, 3))
+    e0.record(st)
+    for _ in range(steps):
+        launch()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    value = symphony_flops(N, D) / (ms * 1e-3) / 1e12
+    print(json.dumps({"impl": "reference", "kind": "reference-gpu-kernel",
+                      "metric": w.get("metric", METRIC), "value": value, "unit": "TFLOPS",
+                      "ms_per_step": ms, "steps": steps, "n_gpus": 1,
+                      "config": {"workload": w["cfg"], "seq_len": N, "head_dim": D}}), flush=True)
+    return 0
+
+
 def _print_reference(args, w, value, sec, desc, threads):
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOPS",
+        "impl": "reference", "metric": w.get("metric", METRIC), "value": value, "unit": "TFLOPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000 * sec, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -273,9 +368,16 @@ def main():
     ap.add_argument("--impl", default="gae", choices=["gae", "reference"])
     ap.add_argument("--workload", default="mha", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reference-kernel", action="store_true",
+                    help="with --impl reference --workload symphony: time the reference's own "
+                         "CUDA kernel (oracle/_ref) instead of the CPU path")
+    ap.add_argument("--seq-len", type=int, default=None,
+                    help="override the workload's sequence length (small profiling cases)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     w = WORKLOADS[args.workload]
+    if args.seq_len:
+        w = dict(w, N=args.seq_len)
     if args.impl == "reference":
         return run_reference(args, w)
 
@@ -309,7 +411,20 @@ def main():
     stream = torch.cuda.current_stream()
     is_int8 = bool(w.get("int8"))
     is_gpt2 = bool(w.get("gpt2"))
-    if is_gpt2:
+    is_sym = bool(w.get("sym"))
+    if is_sym:
+        arrs = symphony_arrays(N, D, 1000 + rank)
+        sd = {n_: torch.from_numpy(a_).to(dev) for n_, a_ in arrs.items()}
+        tf = gae.TuningFork.reference_defaults(D)
+        q, k, v = sd["x"], sd["k"], sd["v"]
+        out = torch.empty_like(q)
+        ws = torch.empty(gae.lib().gae_symphony_workspace_bytes(N, D), dtype=torch.uint8, device=dev)
+        flops = symphony_flops(N, D)
+
+        def run_step(q, k, v):
+            gae.symphony_forward(q, k, v, sd["w_up"], sd["w_down"], sd["n1"], sd["n2"], tf,
+                                 out=out, workspace=ws)
+    elif is_gpt2:
         T = B * N
         L = w["layers"]
         gemm = 2.0 * T * w["d_model"] * (3 * w["d_model"] + w["d_model"] + 2 * w["d_ff"])
@@ -396,6 +511,8 @@ def main():
         launches_per_step = 1
     else:
         launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
+    if is_sym:
+        launches_per_step = 3  # prep, attention, post
 
     # ---- end to end through the public API with host buffers ---------------
     def flat(t):
@@ -478,7 +595,9 @@ def main():
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
-        if w.get("int8"):
+        if is_sym:
+            v_cpu, s_cpu, desc, threads = cpu_sample(w, rows_cap=16384)
+        elif w.get("int8"):
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=2, rows_cap=2048)
         else:
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=None if w["N"] <= 16384 else 2048)
@@ -486,10 +605,11 @@ def main():
                "sample": desc + f" ({s_cpu:.1f} s)"}
 
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOPS", "n_gpus": world,
+        "metric": w.get("metric", METRIC), "value": value, "unit": "TFLOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong" if is_ring else "weak",
-        "vs_baseline": None, "dtype": "int8+bf16" if is_int8 else "bf16",
+        "vs_baseline": None,
+        "dtype": "int8+f16+f32" if is_sym else ("int8+bf16" if is_int8 else "bf16"),
         "data": "synthetic",
         "config": {"workload": w["cfg"], "B": B, "H": H, "seq_len": N, "head_dim": D,
                    "causal": causal, "global_batch": B if is_ring else B * world,

@@ -103,6 +103,9 @@ def lib():
     L.gae_layer_fwd_static.argtypes = [vp, vp, vp]
     L.gae_layernorm_fwd.argtypes = [vp, vp, vp, vp, vp, vp, i64, i64, C.c_float, vp]
     L.gae_linear_fwd.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, vp]
+    L.gae_symphony_workspace_bytes.restype = sz
+    L.gae_symphony_workspace_bytes.argtypes = [i64, i64]
+    L.gae_symphony_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp, vp, sz, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     L.gae_debug_wait_timeout.argtypes = [C.c_uint64, vp]
     _lib = L
@@ -574,3 +577,38 @@ class TransformerBlock:
         mo = linear(hid, bf(self.w2.reshape(m, h).T, (h, m)), bias=fp(self.b2), res=r1)
         out = layernorm_rows(mo, fp(self.ln2_gamma), fp(self.ln2_beta), cfg.eps)
         return out.float().cpu().numpy().reshape(-1)
+
+
+class TuningFork(C.Structure):
+    """Mirror of gae_tuning_fork = the reference's TuningFork
+    (cuda_src/waller_fused_layer.cu:23-32)."""
+    _fields_ = [("attn_scale", C.c_float), ("attn_temperature", C.c_float),
+                ("residual_alpha", C.c_float), ("residual_beta", C.c_float),
+                ("norm_eps", C.c_float), ("activation_type", C.c_int), ("mlp_gate", C.c_float),
+                ("output_scale", C.c_float)]
+
+    @classmethod
+    def reference_defaults(cls, head_dim):
+        """The reference benchmark's settings (waller_fused_layer.cu:311-318)."""
+        return cls(1.0 / (math.sqrt(head_dim) * 127.0 * 127.0), 1.0, 1.0, 1.0, 1e-6, 0, 1.0, 1.0)
+
+
+def symphony_forward(x, k, v, w_up, w_down, norm1_w, norm2_w, tuning: TuningFork, out=None,
+                     workspace=None, stream=None):
+    """The reference's fused symphony layer (cuda_src/waller_fused_layer.cu:64-247)
+    on device tensors: x fp32 [N, d], k/v int8 [N, d], w_up fp32 [d, 4d],
+    w_down fp32 [4d, d], norms fp32 [d].  Returns fp32 [N, d]."""
+    torch = _torch()
+    N, d = x.shape
+    out = torch.empty_like(x) if out is None else out
+    if workspace is None:
+        workspace = torch.empty(lib().gae_symphony_workspace_bytes(N, d), dtype=torch.uint8,
+                                device=x.device)
+    for t in (x, k, v, w_up, w_down, norm1_w, norm2_w, out):
+        if not t.is_contiguous():
+            raise GAEError(1, "symphony_forward: tensors must be contiguous")
+    _check(lib().gae_symphony_fwd(x.data_ptr(), k.data_ptr(), v.data_ptr(), w_up.data_ptr(),
+                                  w_down.data_ptr(), norm1_w.data_ptr(), norm2_w.data_ptr(), N, d,
+                                  C.byref(tuning), out.data_ptr(), workspace.data_ptr(),
+                                  workspace.numel(), _stream_ptr(stream)))
+    return out

@@ -19,6 +19,7 @@
 #include "attn_sm100.cuh"
 #include "attn_int8_sm100.cuh"
 #include "layer_sm100.cuh"
+#include "symphony.cuh"
 
 namespace {
 
@@ -555,6 +556,25 @@ gae_status check_layer(const gae_layer_args *a, const gae_layer_weights *w) {
         if (!q) return fail(GAE_ERR_INVALID_ARG, "NULL layer weight");
     return GAE_OK;
 }
+template <int D>
+gae_status launch_symphony_post(const float *x, const __half *attn, const float *w_up,
+                                      const float *w_down, const float *n1, const float *n2, int64_t n,
+                                      const gae::SymTuning &t, float *out, cudaStream_t st) {
+    using P = gae::SymPost<D>;
+    static bool configured[64] = {};
+    int dev = 0;
+    GAE_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 64 && !configured[dev]) {
+        GAE_CUDA_TRY(cudaFuncSetAttribute(gae::symphony_post_kernel<D>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P::kSmem));
+        configured[dev] = true;
+    }
+    const unsigned blocks = (unsigned)((n + P::T - 1) / P::T);
+    gae::symphony_post_kernel<D><<<blocks, P::kThreads, P::kSmem, st>>>(x, attn, w_up, w_down, n1, n2, n, t, out);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
 }  // namespace
 
 // ==================================================================== C ABI
@@ -707,6 +727,58 @@ gae_status gae_layer_stack_fwd(const gae_layer_args *a, const gae_layer_weights 
         if ((s = layer_once(a, w + i, cur, nxt, st)) != GAE_OK) return s;
         cur = nxt;
     }
+    return GAE_OK;
+}
+
+size_t gae_symphony_workspace_bytes(int64_t seq_len, int64_t head_dim) {
+    if (seq_len < 1 || head_dim < 1) return 0;
+    const size_t region = ((size_t)seq_len * head_dim * 2 + 255) & ~(size_t)255;
+    return 4 * region;  // q, k, v (f16) and the attention output (f16)
+}
+
+gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v, const float *w_up,
+                            const float *w_down, const float *norm1_w, const float *norm2_w,
+                            int64_t n, int64_t d, const gae_tuning_fork *tf, float *output,
+                            void *workspace, size_t workspace_bytes, void *stream) {
+    if (n == 0) return GAE_OK;
+    if (!input || !k || !v || !w_up || !w_down || !norm1_w || !norm2_w || !tf || !output || !workspace)
+        return fail(GAE_ERR_INVALID_ARG, "NULL pointer in symphony arguments");
+    if (n < 0 || (d != 64 && d != 128)) return fail(GAE_ERR_UNSUPPORTED, "symphony supports head_dim 64 or 128");
+    if (tf->activation_type < 0 || tf->activation_type > 2) return fail(GAE_ERR_INVALID_ARG, "activation_type must be 0, 1 or 2");
+    if (!(tf->attn_temperature != 0.f)) return fail(GAE_ERR_INVALID_ARG, "attn_temperature is zero");
+    const size_t need = gae_symphony_workspace_bytes(n, d);
+    if (workspace_bytes < need) return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", workspace_bytes, need);
+    if (!aligned16(workspace) || !aligned16(input) || !aligned16(output) || !aligned16(w_up) || !aligned16(w_down))
+        return fail(GAE_ERR_INVALID_ARG, "symphony: input, output, weights and workspace must be 16-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const size_t region = need / 4;
+    char *ws = static_cast<char *>(workspace);
+    __half *qh = (__half *)ws, *kh = (__half *)(ws + region), *vh = (__half *)(ws + 2 * region),
+           *oh = (__half *)(ws + 3 * region);
+    const int64_t elems = n * d;
+    gae::symphony_prep_kernel<<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(input, k, v, qh, kh, vh, elems);
+    GAE_CUDA_TRY(cudaGetLastError());
+    gae_attn_args a;
+    memset(&a, 0, sizeof(a));
+    a.q = qh; a.k = kh; a.v = vh; a.o = oh;
+    a.batch = 1; a.heads = 1; a.seq_q = n; a.seq_kv = n; a.head_dim = d;
+    const int64_t str[3] = {n * d, n * d, d};
+    memcpy(a.q_stride, str, sizeof str); memcpy(a.k_stride, str, sizeof str);
+    memcpy(a.v_stride, str, sizeof str); memcpy(a.o_stride, str, sizeof str);
+    a.dtype = GAE_DTYPE_F16;
+    a.causal = 1;
+    a.scale = tf->attn_scale / tf->attn_temperature;
+    if (!(a.scale >= 0.f)) return fail(GAE_ERR_UNSUPPORTED, "attn_scale / attn_temperature must be >= 0");
+    gae_status s = launch_attn_tc(&a, st);
+    if (s != GAE_OK) return s;
+    gae::SymTuning t;
+    t.attn_scale = tf->attn_scale; t.attn_temperature = tf->attn_temperature;
+    t.residual_alpha = tf->residual_alpha; t.residual_beta = tf->residual_beta; t.norm_eps = tf->norm_eps;
+    t.activation_type = tf->activation_type; t.mlp_gate = tf->mlp_gate; t.output_scale = tf->output_scale;
+    if (d == 64) s = launch_symphony_post<64>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
+    else s = launch_symphony_post<128>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
+    if (s != GAE_OK) return s;
+    GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }
 

@@ -1,0 +1,202 @@
+// symphony.cuh -- the reference's fused "symphony" layer mode
+// (cuda_src/waller_fused_layer.cu:64-247, knobs in TuningFork :23-32) on B200.
+//
+// The reference runs one thread per token through the whole layer.  Here:
+//   1. symphony_prep_kernel: Q = trunc(clamp(x * 127, +-127)) (the identity
+//      projection of :113-118); Q, K, V int8 values widened to f16 -- exact,
+//      so the f16 tensor-core attention kernel computes the int32 dot products
+//      of :156-160 exactly (|dot| <= 127*128*256 < 2^24 in fp32 accumulation).
+//   2. attn_fwd_sm100_kernel (f16 mode, causal, scale = attn_scale /
+//      temperature): the online-softmax attention of :123-185 with the integer
+//      V of the reference (not de-scaled).
+//   3. symphony_post_kernel: a tile of tokens per CTA through the gated
+//      residual, RMSNorm, MLP (W_up [d, 4d] -> activation -> W_down [4d, d],
+//      * gate), gated residual, RMSNorm and output scale of :190-246, fp32 on
+//      the CUDA cores (register-tiled, activations in shared memory; the MLP
+//      is 2 x d x 4d MACs per token, a few percent of the attention's cost).
+#pragma once
+#include "sm100.cuh"
+
+namespace gae {
+
+struct SymTuning {
+    float attn_scale, attn_temperature, residual_alpha, residual_beta, norm_eps;
+    int activation_type;
+    float mlp_gate, output_scale;
+};
+
+__global__ void symphony_prep_kernel(const float *x, const int8_t *k, const int8_t *v, __half *qh,
+                                     __half *kh, __half *vh, int64_t n_elems) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_elems) return;
+    // (int8_t) of a float truncates toward zero, as the reference's cast does.
+    const int q = (int)fmaxf(-127.0f, fminf(127.0f, x[i] * 127.0f));
+    qh[i] = __int2half_rn(q);
+    kh[i] = __int2half_rn((int)k[i]);
+    vh[i] = __int2half_rn((int)v[i]);
+}
+
+__device__ __forceinline__ float sym_activation(float x, int type) {
+    switch (type) {
+        case 0: return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+        case 1: return x / (1.0f + expf(-x));
+        case 2: return x > 0.0f ? x * x : 0.0f;
+        default: return x;
+    }
+}
+
+// Post kernel tiling: T tokens per CTA (64 at head_dim 64, 32 at 128), 256
+// threads, 8 warps.  Both projections are register-tiled outer products over
+// transposed shared-memory operands, so that a warp's loads per k-step are a
+// few 128-byte wavefronts for 16-64 FMA instructions:
+//   up   [T, D] x [D, 4D]: warp tile 32 tokens x 64 columns, lane tile 8 x 8
+//        (lane = 4 token groups x 8 column groups);
+//   down [T, 4D] x [4D, D]: warp tile 16 tokens x 32 columns, lane tile 4 x 4.
+// Weights stream from L2/L1 as float4 (a CTA reads them once per T tokens).
+template <int D> struct SymPost {
+    static constexpr int M = 4 * D;
+    static constexpr int T = D == 64 ? 64 : 32;
+    static constexpr int kThreads = 256;
+    static constexpr int kTP = T + 4;  // pitch (floats) of the token-minor buffers
+    static constexpr int kUpWarpsT = T / 32, kUpWarpsC = 8 / kUpWarpsT;  // 64-column strips
+    static constexpr int kDnWarpsT = T / 16, kDnWarpsC = 8 / kDnWarpsT;  // 32-column strips
+    static_assert(kUpWarpsC * 64 == M, "up tiling");
+    static_assert(kDnWarpsC * 32 == D, "down tiling");
+    static constexpr size_t kSmem = sizeof(float) * ((size_t)T * D + (size_t)D * kTP + (size_t)M * kTP);
+};
+
+template <int D>
+__global__ void __launch_bounds__(256, 2) symphony_post_kernel(const float *x, const __half *attn,
+                                                               const float *w_up, const float *w_down,
+                                                               const float *n1, const float *n2, int64_t n,
+                                                               SymTuning tf, float *out) {
+    using P = SymPost<D>;
+    constexpr int M = P::M, T = P::T, TP = P::kTP;
+    extern __shared__ __align__(16) float sym_smem[];
+    float *st = sym_smem;           // [T][D]: state (residual 1 -> norm 1 -> residual 2 -> norm 2)
+    float *stT = st + T * D;        // [D][TP]: normed state, token-minor (up-projection operand)
+    float *hidT = stT + D * TP;     // [M][TP]: activated hidden, token-minor (down operand)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t row0 = (int64_t)blockIdx.x * T;
+
+    // Residual 1 (reference :190-194), four elements a thread per step.
+#pragma unroll
+    for (int i4 = tid; i4 < T * D / 4; i4 += P::kThreads) {
+        const int i = 4 * i4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row0 + i / D < n) {
+            const float4 xv = __ldg(reinterpret_cast<const float4 *>(x + row0 * D + i));
+            const uint2 ah = *reinterpret_cast<const uint2 *>(attn + row0 * D + i);
+            const float2 a01 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.x));
+            const float2 a23 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.y));
+            v = make_float4(xv.x * tf.residual_alpha + a01.x, xv.y * tf.residual_alpha + a01.y,
+                            xv.z * tf.residual_alpha + a23.x, xv.w * tf.residual_alpha + a23.y);
+        }
+        *reinterpret_cast<float4 *>(st + i) = v;
+    }
+    __syncthreads();
+    // RMSNorm of one token row per warp pass (reference :49-60).
+    auto rmsnorm = [&](const float *w, float post, bool transpose) {
+        for (int t = warp; t < T; t += 8) {
+            float *row = st + t * D;
+            float ss = 0.f;
+#pragma unroll
+            for (int c = lane; c < D; c += 32) ss += row[c] * row[c];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float scale = rsqrtf(ss / (float)D + tf.norm_eps);
+#pragma unroll
+            for (int c = lane; c < D; c += 32) {
+                const float v = row[c] * scale * __ldg(w + c) * post;
+                row[c] = v;
+                if (transpose) stT[c * TP + t] = v;
+            }
+        }
+    };
+    rmsnorm(n1, 1.f, true);
+    __syncthreads();
+
+    // Up projection + activation (reference :207-218).
+    {
+        const int t0 = (warp % P::kUpWarpsT) * 32 + (lane >> 3) * 8;
+        const int j0 = (warp / P::kUpWarpsT) * 64 + (lane & 7) * 8;
+        float acc[8][8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a)
+#pragma unroll
+            for (int b = 0; b < 8; ++b) acc[a][b] = 0.f;
+        // Weight rows are prefetched one k-step ahead: the L1/L2 load latency
+        // of the next row hides behind this row's 64 FMAs.
+        const float *wp = w_up + j0;
+        float4 w0 = __ldg(reinterpret_cast<const float4 *>(wp));
+        float4 w1 = __ldg(reinterpret_cast<const float4 *>(wp + 4));
+#pragma unroll 2
+        for (int c = 0; c < D; ++c) {
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+            const int cn = c + 1 < D ? c + 1 : c;
+            w0 = __ldg(reinterpret_cast<const float4 *>(wp + (size_t)cn * M));
+            w1 = __ldg(reinterpret_cast<const float4 *>(wp + (size_t)cn * M + 4));
+            const float4 s0 = *reinterpret_cast<const float4 *>(stT + c * TP + t0);
+            const float4 s1 = *reinterpret_cast<const float4 *>(stT + c * TP + t0 + 4);
+            const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+            for (int a = 0; a < 8; ++a)
+#pragma unroll
+                for (int b = 0; b < 8; ++b) acc[a][b] = fmaf(sv[a], wv[b], acc[a][b]);
+        }
+#pragma unroll
+        for (int b = 0; b < 8; ++b) {
+            float h[8];
+#pragma unroll
+            for (int a = 0; a < 8; ++a) h[a] = sym_activation(acc[a][b], tf.activation_type);
+            float *dst = hidT + (j0 + b) * TP + t0;
+            *reinterpret_cast<float4 *>(dst) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4 *>(dst + 4) = make_float4(h[4], h[5], h[6], h[7]);
+        }
+    }
+    __syncthreads();
+
+    // Down projection * gate, then residual 2 in place (reference :220-238).
+    {
+        const int t0 = (warp % P::kDnWarpsT) * 16 + (lane >> 3) * 4;
+        const int c0 = (warp / P::kDnWarpsT) * 32 + (lane & 7) * 4;
+        float acc[4][4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[a][b] = 0.f;
+        const float *wp = w_down + c0;
+        float4 wn[2] = {__ldg(reinterpret_cast<const float4 *>(wp)),
+                        __ldg(reinterpret_cast<const float4 *>(wp + D))};
+#pragma unroll 4
+        for (int i = 0; i < M; ++i) {
+            const float4 w = wn[i & 1];
+            const int in = i + 2 < M ? i + 2 : i;
+            wn[i & 1] = __ldg(reinterpret_cast<const float4 *>(wp + (size_t)in * D));
+            const float4 h = *reinterpret_cast<const float4 *>(hidT + i * TP + t0);
+            const float hv[4] = {h.x, h.y, h.z, h.w}, wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(hv[a], wv[b], acc[a][b]);
+        }
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                float *p = st + (t0 + a) * D + c0 + b;
+                *p = *p * tf.residual_beta + acc[a][b] * tf.mlp_gate;
+            }
+    }
+    __syncthreads();
+    rmsnorm(n2, tf.output_scale, false);  // reference :239-246
+    __syncthreads();
+#pragma unroll
+    for (int i4 = tid; i4 < T * D / 4; i4 += P::kThreads) {
+        const int i = 4 * i4;
+        if (row0 + i / D < n)
+            *reinterpret_cast<float4 *>(out + row0 * D + i) = *reinterpret_cast<const float4 *>(st + i);
+    }
+}
+
+}  // namespace gae

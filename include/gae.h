@@ -255,6 +255,39 @@ GAE_API gae_status gae_layer_fwd_static(const gae_layer_args *args, const gae_la
 GAE_API gae_status gae_linear_fwd(const void *x, const void *w, const float *bias, const void *res,
                                   void *y, int64_t M, int64_t N, int64_t K, int epilogue, void *stream);
 
+/* ------------------------------------------------------------------------
+ * The reference's fused "symphony" layer (cuda_src/waller_fused_layer.cu:
+ * 64-247; its knobs are the TuningFork struct, :23-32, mirrored field by
+ * field): per token, Q = trunc(clamp(x*127, +-127)) (identity projection),
+ * causal attention with int8 K and the integer values of int8 V,
+ * score = dot * attn_scale / attn_temperature; state = x*residual_alpha +
+ * attn -> RMSNorm(norm1_w, norm_eps) -> MLP (x @ w_up [d, 4d], activation
+ * 0 GELU-tanh / 1 SiLU / 2 ReLU^2, @ w_down [4d, d], * mlp_gate) ->
+ * state*residual_beta + mlp -> RMSNorm(norm2_w) -> * output_scale.
+ * input/output fp32 [seq_len, head_dim], k/v int8 [seq_len, head_dim], weights
+ * fp32 row-major; head_dim 64 or 128; input, output, w_up, w_down and the
+ * workspace 16-byte aligned.  `workspace`: device memory of at least
+ * gae_symphony_workspace_bytes(seq_len, head_dim) bytes.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    float attn_scale;
+    float attn_temperature;
+    float residual_alpha;
+    float residual_beta;
+    float norm_eps;
+    int activation_type;
+    float mlp_gate;
+    float output_scale;
+} gae_tuning_fork;
+
+GAE_API size_t gae_symphony_workspace_bytes(int64_t seq_len, int64_t head_dim);
+
+GAE_API gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v,
+                                    const float *w_up, const float *w_down, const float *norm1_w,
+                                    const float *norm2_w, int64_t seq_len, int64_t head_dim,
+                                    const gae_tuning_fork *tuning, float *output, void *workspace,
+                                    size_t workspace_bytes, void *stream);
+
 /* Row LayerNorm with the reference's semantics (population variance, eps
  * inside the sqrt; rust_src/src/layernorm.rs:20-47): bf16 in/out, fp32
  * gamma/beta, optional fused residual add (res may be NULL: y = LN(x);

@@ -538,3 +538,85 @@ int ora_num_threads(void) {
     return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------------ */
+/* Fused "symphony" layer (cuda_src/waller_fused_layer.cu:64-247): one token  */
+/* through identity-Q int8 causal attention, a gated residual, RMSNorm, an    */
+/* MLP with a selectable activation, a gated residual and RMSNorm.  tf holds  */
+/* the TuningFork fields (waller_fused_layer.cu:23-32) in order: attn_scale,  */
+/* attn_temperature, residual_alpha, residual_beta, norm_eps, mlp_gate,       */
+/* output_scale; act is activation_type (0 GELU-tanh, 1 SiLU, 2 ReLU^2).      */
+/* input/output [n, d] fp32, k/v int8 [n, d], w_up [d, 4d], w_down [4d, d].   */
+/* ------------------------------------------------------------------------ */
+static float sym_act(float x, int type) {  /* waller_fused_layer.cu:35-46 */
+    switch (type) {
+        case 0: return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
+        case 1: return x / (1.0f + expf(-x));
+        case 2: return x > 0.0f ? x * x : 0.0f;
+        default: return x;
+    }
+}
+
+static void sym_rmsnorm(float *x, const float *w, size_t d, float eps) {  /* :49-60 */
+    float ss = 0.0f;
+    for (size_t i = 0; i < d; ++i) ss += x[i] * x[i];
+    float scale = 1.0f / sqrtf(ss / (float)d + eps);
+    for (size_t i = 0; i < d; ++i) x[i] = x[i] * scale * w[i];
+}
+
+void ora_symphony_layer(const float *input, const int8_t *k, const int8_t *v, const float *w_up,
+                        const float *w_down, const float *n1, const float *n2, size_t n, size_t d,
+                        const float *tf, int act, float *out) {
+    const float attn_scale = tf[0], temp = tf[1], alpha = tf[2], beta = tf[3], eps = tf[4];
+    const float gate = tf[5], oscale = tf[6];
+    const size_t m = 4 * d;
+    #pragma omp parallel
+    {
+        float *state = (float *)malloc(d * sizeof(float));
+        float *res = (float *)malloc(d * sizeof(float));
+        float *acc = (float *)malloc(d * sizeof(float));
+        float *hid = (float *)malloc(m * sizeof(float));
+        int8_t *q = (int8_t *)malloc(d);
+        #pragma omp for schedule(dynamic, 16)
+        for (size_t row = 0; row < n; ++row) {
+            for (size_t c = 0; c < d; ++c) { state[c] = input[row * d + c]; res[c] = state[c]; }
+            /* :113-118 identity projection, quantised by truncation */
+            for (size_t c = 0; c < d; ++c) q[c] = (int8_t)fmaxf(-127.0f, fminf(127.0f, state[c] * 127.0f));
+            /* :123-185 causal attention, per-key online softmax */
+            float mx = -INFINITY, sum = 0.0f;
+            for (size_t c = 0; c < d; ++c) acc[c] = 0.0f;
+            for (size_t j = 0; j <= row; ++j) {
+                int32_t dot = 0;
+                for (size_t c = 0; c < d; ++c) dot += (int32_t)q[c] * (int32_t)k[j * d + c];
+                float score = (float)dot * attn_scale / temp;
+                float old = mx;
+                mx = fmaxf(mx, score);
+                float resc = expf(old - mx);
+                sum = sum * resc + expf(score - mx);
+                float w = expf(score - mx);
+                for (size_t c = 0; c < d; ++c) acc[c] = acc[c] * resc + w * (float)v[j * d + c];
+            }
+            float inv = 1.0f / sum;
+            /* :190-194 */
+            for (size_t c = 0; c < d; ++c) state[c] = res[c] * alpha + acc[c] * inv;
+            sym_rmsnorm(state, n1, d, eps);
+            for (size_t c = 0; c < d; ++c) res[c] = state[c];
+            /* :207-229 */
+            for (size_t i = 0; i < m; ++i) {
+                float s = 0.0f;
+                for (size_t c = 0; c < d; ++c) s += state[c] * w_up[c * m + i];
+                hid[i] = sym_act(s, act);
+            }
+            for (size_t c = 0; c < d; ++c) {
+                float s = 0.0f;
+                for (size_t i = 0; i < m; ++i) s += hid[i] * w_down[i * d + c];
+                acc[c] = s * gate;
+            }
+            /* :234-246 */
+            for (size_t c = 0; c < d; ++c) state[c] = res[c] * beta + acc[c];
+            sym_rmsnorm(state, n2, d, eps);
+            for (size_t c = 0; c < d; ++c) out[row * d + c] = state[c] * oscale;
+        }
+        free(state); free(res); free(acc); free(hid); free(q);
+    }
+}

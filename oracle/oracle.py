@@ -28,7 +28,27 @@ _sz = C.c_size_t
 def build() -> str:
     """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    ref_src = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference", "cuda_src",
+                           "waller_fused_layer.cu")
+    if os.path.exists(ref_src):  # the reference tree exists only where it is checked out
+        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
     return _LIB_PATH
+
+
+REF_SYMPHONY_PATH = os.path.join(_HERE, "_ref", "libref_symphony.so")
+
+
+def ref_symphony():
+    """ctypes handle on the reference's own symphony kernel built from its
+    source (oracle/ref_symphony.cu), or None where it was not built.  Takes
+    device pointers: ref_symphony_fwd(k, v, w_up, w_down, n1, n2, input,
+    output, seq_len, tf[7] host array, act, stream)."""
+    if not os.path.exists(REF_SYMPHONY_PATH):
+        return None
+    L = C.CDLL(REF_SYMPHONY_PATH)
+    vp = C.c_void_p
+    L.ref_symphony_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, C.c_int, _f32p, C.c_int, vp]
+    return L
 
 
 class _Softmax(C.Structure):
@@ -81,6 +101,8 @@ def lib():
         C.c_void_p, _sz, _f32p]
     L.ora_gpt2_layer.argtypes = (
         [_f32p, _sz, _sz, _sz, _sz, _sz, C.c_float] + [_f32p] * 12 + [C.c_int, _f32p])
+    L.ora_symphony_layer.argtypes = [_f32p, _i8p, _i8p, _f32p, _f32p, _f32p, _f32p, _sz, _sz,
+                                     _f32p, C.c_int, _f32p]
     L.ora_num_threads.restype = C.c_int
     _lib = L
     return L
@@ -280,3 +302,15 @@ def gpt2_layer(x, B, S, D, nh, F, eps, w, round_bf16=True):
 
 def num_threads() -> int:
     return lib().ora_num_threads()
+
+
+def symphony_layer(x, k, v, w_up, w_down, n1, n2, tuning, act=0):
+    """cuda_src/waller_fused_layer.cu:64-247.  tuning = (attn_scale, temperature,
+    alpha, beta, eps, mlp_gate, output_scale)."""
+    x = _f32(x)
+    n, d = x.shape
+    out = np.empty_like(x)
+    lib().ora_symphony_layer(x, np.ascontiguousarray(k, np.int8), np.ascontiguousarray(v, np.int8),
+                             _f32(w_up), _f32(w_down), _f32(n1), _f32(n2), n, d,
+                             _f32(np.asarray(tuning, np.float32)), int(act), out)
+    return out

@@ -105,3 +105,18 @@ def test_scalar_helpers_match_reference_kats(gae):
     assert (llama.hidden_dim, llama.num_heads, llama.head_dim) == (4096, 32, 128)
     with pytest.raises(gae.GAEError):
         gae.GAEConfig.new(100, 3, 400, 16)
+
+
+def test_symphony_workspace_and_rejections(gae):
+    L = gae.lib()
+    assert L.gae_symphony_workspace_bytes(1000, 64) == 4 * ((1000 * 64 * 2 + 255) // 256 * 256)
+    assert L.gae_symphony_workspace_bytes(0, 64) == 0
+    tf = gae.TuningFork.reference_defaults(64)
+    assert L.gae_symphony_fwd(None, None, None, None, None, None, None, 16, 64, C.byref(tf),
+                              None, None, 0, None) == 1
+    p = 1 << 20
+    assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 96, C.byref(tf), p, p, 1 << 30, None) == 2
+    tf.activation_type = 3
+    assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 1 << 30, None) == 1
+    tf.activation_type = 0
+    assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 16, None) == 1
