@@ -506,6 +506,52 @@ class Gpt2Layer:
                                      ln2_gamma=o(D), ln2_beta=z(D), w_fc=mk(F, D), b_fc=z(F),
                                      w_fc2=mk(D, F), b_fc2=z(D)), eps)
 
+    # Raw-weight file stems (GPT-2 module names: attn.c_attn, attn.c_proj,
+    # mlp.c_fc, mlp.c_proj, ln_1, ln_2) -> layer tensor.  The reference ships
+    # `layer_weights/{b_fc,b_proj}_layer{0..11}.bin` (3072 and 768 f32 each; its
+    # large matrices are not distributed), i.e. the MLP pair c_fc / c_proj.
+    FILE_MAP = {"ln_1_g": "ln1_gamma", "ln_1_b": "ln1_beta", "w_attn": "w_qkv",
+                "b_attn": "b_qkv", "w_attn_proj": "w_proj", "b_attn_proj": "b_proj",
+                "ln_2_g": "ln2_gamma", "ln_2_b": "ln2_beta", "w_fc": "w_fc", "b_fc": "b_fc",
+                "w_proj": "w_fc2", "b_proj": "b_fc2"}
+
+    def load_weights(self, directory, layer_index, file_map=None):
+        """Overwrites this layer's tensors with the raw little-endian f32 files
+        `<stem>_layer<layer_index>.bin` present in `directory` (stems from
+        `file_map`, default FILE_MAP).  Matrices are stored as GPT-2 keeps
+        them, [in, out], and are transposed to this layer's [out, in].  Files
+        that are absent leave the tensor as it was; a file whose size does not
+        match raises GAEError(GAE_ERR_INVALID_ARG).  Returns the loaded names."""
+        torch = _torch()
+        loaded = []
+        for stem, name in (file_map or self.FILE_MAP).items():
+            path = os.path.join(directory, f"{stem}_layer{layer_index}.bin")
+            if not os.path.exists(path):
+                continue
+            dst = self.w[name]
+            raw = np.fromfile(path, dtype="<f4")
+            if raw.size != dst.numel():
+                raise GAEError(1, f"{path}: {raw.size} floats, {name} needs {dst.numel()}")
+            t = torch.from_numpy(raw.astype(np.float32))
+            if dst.dim() == 2:
+                t = t.reshape(dst.shape[1], dst.shape[0]).t()
+            dst.copy_(t.reshape(dst.shape).to(dst.dtype))
+            loaded.append(name)
+        return loaded
+
+    @classmethod
+    def load_stack(cls, directory, n_layers, d_model, heads, d_ff, device="cuda", seed=0,
+                   eps=1e-5, file_map=None):
+        """n_layers layers initialised as `random` (seed + layer index), then
+        every weight file present in `directory` loaded over them.  Returns
+        (layers, {layer index: loaded names})."""
+        layers, report = [], {}
+        for i in range(n_layers):
+            layer = cls.random(d_model, heads, d_ff, device=device, seed=seed + i, eps=eps)
+            report[i] = layer.load_weights(directory, i, file_map)
+            layers.append(layer)
+        return layers, report
+
     def _args(self, x, out, ws):
         B, S, D = x.shape
         return LayerArgs(x.data_ptr(), out.data_ptr(), B, S, D, self.heads, self.d_ff, self.eps,
