@@ -60,6 +60,22 @@ class AttnArgs(C.Structure):
     ]
 
 
+class AttnBwdArgs(C.Structure):
+    """Mirror of gae_attn_bwd_args (include/gae.h)."""
+    _fields_ = [
+        ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p), ("o", C.c_void_p),
+        ("dout", C.c_void_p), ("lse", C.c_void_p), ("dq", C.c_void_p), ("dk", C.c_void_p),
+        ("dv", C.c_void_p),
+        ("batch", C.c_int64), ("heads", C.c_int64), ("seq_q", C.c_int64),
+        ("seq_kv", C.c_int64), ("head_dim", C.c_int64),
+        ("q_stride", C.c_int64 * 3), ("k_stride", C.c_int64 * 3), ("v_stride", C.c_int64 * 3),
+        ("o_stride", C.c_int64 * 3), ("do_stride", C.c_int64 * 3), ("dq_stride", C.c_int64 * 3),
+        ("dk_stride", C.c_int64 * 3), ("dv_stride", C.c_int64 * 3),
+        ("dtype", C.c_int), ("causal", C.c_int), ("scale", C.c_float),
+        ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
 class AttnInt8Args(C.Structure):
     """Mirror of gae_attn_int8_args (include/gae.h)."""
     _fields_ = [
@@ -92,6 +108,9 @@ def lib():
     L.gae_waller_operator_parallel_f32_host.argtypes = host
     L.gae_standard_attention_f32_host.argtypes = host
     L.gae_attn_fwd.argtypes = [C.POINTER(AttnArgs), vp]
+    L.gae_attn_bwd.argtypes = [C.POINTER(AttnBwdArgs), vp]
+    L.gae_attn_bwd_workspace_bytes.restype = sz
+    L.gae_attn_bwd_workspace_bytes.argtypes = [i64, i64, i64, i64]
     L.gae_attn_int8_fwd.argtypes = [C.POINTER(AttnInt8Args), vp]
     L.gae_int8_logits.argtypes = [vp, vp, i64, i64, i64, i64, vp, vp]
     L.gae_quantize_rows_int8.argtypes = [vp, C.c_int, i64, i64, vp, vp, vp]
@@ -196,6 +215,79 @@ def attention(q, k, v, *, causal: bool = False, scale: float | None = None, q_of
     a.q_offset, a.kv_offset = int(q_offset), int(kv_offset)
     _check(lib().gae_attn_fwd(C.byref(a), _stream_ptr(stream)))
     return (out, lse) if return_lse else out
+
+
+def attention_backward(q, k, v, out, dout, lse, *, causal: bool = False, scale: float | None = None,
+                       dq=None, dk=None, dv=None, workspace=None, stream=None):
+    """Gradients (dq, dk, dv) of attention(q, k, v, causal, scale) = out given
+    dout, from the forward's lse ([B, H, Nq] fp32, return_lse=True).  bf16/f16
+    tensors [B, H, N, D] (strided views allowed), head_dim 64/128; causal
+    needs Nq == Nkv.  The reference is inference-only: this is the training
+    caller of its operator (gae_attn_bwd)."""
+    torch = _torch()
+    B, H, Nq, D = q.shape
+    Nkv = k.shape[2]
+    if k.shape != (B, H, Nkv, D) or v.shape != k.shape or out.shape != q.shape or dout.shape != q.shape:
+        raise GAEError(1, "attention_backward: shape mismatch")
+    if len({t.dtype for t in (q, k, v, out, dout)}) != 1:
+        raise GAEError(1, "attention_backward: q, k, v, out, dout must share a dtype")
+    if lse.dtype != torch.float32 or not lse.is_contiguous() or lse.numel() != B * H * Nq:
+        raise GAEError(1, "attention_backward: lse must be contiguous fp32 [B, H, Nq]")
+    dq = torch.empty_like(q, memory_format=torch.contiguous_format) if dq is None else dq
+    dk = torch.empty_like(k, memory_format=torch.contiguous_format) if dk is None else dk
+    dv = torch.empty_like(v, memory_format=torch.contiguous_format) if dv is None else dv
+    if workspace is None:
+        workspace = torch.empty(lib().gae_attn_bwd_workspace_bytes(B, H, Nq, D), dtype=torch.uint8,
+                                device=q.device)
+    a = AttnBwdArgs()
+    a.q, a.k, a.v, a.o, a.dout = (t.data_ptr() for t in (q, k, v, out, dout))
+    a.lse = lse.data_ptr()
+    a.dq, a.dk, a.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    a.batch, a.heads, a.seq_q, a.seq_kv, a.head_dim = B, H, Nq, Nkv, D
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", out), ("do", dout), ("dq", dq), ("dk", dk),
+                    ("dv", dv)):
+        getattr(a, name + "_stride")[:] = _bhsd(t, name)
+    a.dtype = _dtype_code(q)
+    a.causal = 1 if causal else 0
+    a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    a.workspace, a.workspace_bytes = workspace.data_ptr(), workspace.numel()
+    _check(lib().gae_attn_bwd(C.byref(a), _stream_ptr(stream)))
+    return dq, dk, dv
+
+
+def _attention_function():
+    torch = _torch()
+
+    class AttentionFunction(torch.autograd.Function):
+        """torch.autograd wrapper: forward = gae_attn_fwd (saves the LSE),
+        backward = gae_attn_bwd."""
+
+        @staticmethod
+        def forward(ctx, q, k, v, causal, scale):
+            out, lse = attention(q, k, v, causal=causal, scale=scale, return_lse=True)
+            ctx.save_for_backward(q, k, v, out, lse)
+            ctx.causal, ctx.scale = causal, scale
+            return out
+
+        @staticmethod
+        def backward(ctx, dout):
+            q, k, v, out, lse = ctx.saved_tensors
+            dq, dk, dv = attention_backward(q, k, v, out, dout.contiguous(), lse, causal=ctx.causal,
+                                            scale=ctx.scale)
+            return dq, dk, dv, None, None
+
+    return AttentionFunction
+
+
+_ATTN_FN = None
+
+
+def attention_autograd(q, k, v, *, causal: bool = False, scale: float | None = None):
+    """attention() that records a backward (training use)."""
+    global _ATTN_FN
+    if _ATTN_FN is None:
+        _ATTN_FN = _attention_function()
+    return _ATTN_FN.apply(q, k, v, causal, scale)
 
 
 def lse_merge_(o_acc, lse_acc, o_part, lse_part, stream=None):

@@ -17,6 +17,7 @@
 #include "../../include/gae_debug.h"
 #include "attn_f32.cuh"
 #include "attn_sm100.cuh"
+#include "attn_bwd_sm100.cuh"
 #include "attn_int8_sm100.cuh"
 #include "layer_sm100.cuh"
 #include "symphony.cuh"
@@ -198,6 +199,104 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
         else s = launch_tc<64, gae::kModeF16>(p, grid, st);
     }
     return s;
+}
+
+size_t attn_bwd_ws_region(int64_t B, int64_t H, int64_t N, int64_t D) {
+    return ((size_t)(B * H * N * D) * 4 + 255) & ~(size_t)255;
+}
+
+template <int D, bool kBF16>
+gae_status launch_bwd_tc(const gae::AttnBwdParams &p, dim3 grid, cudaStream_t st) {
+    auto kern = gae::attn_bwd_sm100_kernel<D, kBF16>;
+    constexpr int smem = gae::AttnBwdCfg<D>::kSmemBytes;
+    gae_status s = set_smem(kern, smem);
+    if (s != GAE_OK) return s;
+    kern<<<grid, gae::AttnBwdCfg<D>::kThreads, smem, st>>>(p);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status launch_attn_bwd(const gae_attn_bwd_args *a, cudaStream_t st) {
+    const int64_t B = a->batch, H = a->heads, Nq = a->seq_q, Nkv = a->seq_kv, D = a->head_dim;
+    if (B < 1 || H < 1 || Nq < 1 || Nkv < 1) return fail(GAE_ERR_INVALID_ARG, "empty or negative shape");
+    if (D != 64 && D != 128)
+        return fail(GAE_ERR_UNSUPPORTED, "attention backward supports head_dim 64 or 128, got %lld", (long long)D);
+    if (a->dtype != GAE_DTYPE_BF16 && a->dtype != GAE_DTYPE_F16)
+        return fail(GAE_ERR_UNSUPPORTED, "attention backward supports bf16 and f16");
+    if (a->causal && Nq != Nkv) return fail(GAE_ERR_UNSUPPORTED, "causal backward needs seq_q == seq_kv");
+    if (B * H > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch*heads > 65535");
+    if (Nq > (1ll << 30) || Nkv > (1ll << 30)) return fail(GAE_ERR_UNSUPPORTED, "sequence longer than 2^30");
+    if (!(a->scale >= 0.f)) return fail(GAE_ERR_UNSUPPORTED, "negative or NaN scale");
+    const void *ptrs[10] = {a->q, a->k, a->v, a->o, a->dout, a->lse, a->dq, a->dk, a->dv, a->workspace};
+    for (const void *pp : ptrs)
+        if (!pp) return fail(GAE_ERR_INVALID_ARG, "NULL pointer in attention backward arguments");
+        else if (!aligned16(pp)) return fail(GAE_ERR_INVALID_ARG, "attention backward pointers must be 16-byte aligned");
+    const int64_t *strs[8] = {a->q_stride, a->k_stride, a->v_stride, a->o_stride,
+                              a->do_stride, a->dq_stride, a->dk_stride, a->dv_stride};
+    for (const int64_t *sp : strs)
+        for (int i = 0; i < 3; ++i)
+            if (sp[i] < 0 || (sp[i] % 8) != 0)
+                return fail(GAE_ERR_INVALID_ARG, "strides must be non-negative multiples of 8 elements");
+    const size_t need = gae_attn_bwd_workspace_bytes(B, H, Nq, D);
+    if (a->workspace_bytes < need)
+        return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", a->workspace_bytes, need);
+
+    const bool bf16 = a->dtype == GAE_DTYPE_BF16;
+    float *dq_acc = static_cast<float *>(a->workspace);
+    float *delta = reinterpret_cast<float *>(static_cast<char *>(a->workspace) + attn_bwd_ws_region(B, H, Nq, D));
+    GAE_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)(B * H * Nq * D) * 4, st));
+    {
+        const int64_t rows = B * H * Nq;
+        const unsigned blocks = (unsigned)((rows + 7) / 8);
+        if (bf16)
+            gae::attn_bwd_delta_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+                (const __nv_bfloat16 *)a->o, (const __nv_bfloat16 *)a->dout, delta, (int)B, (int)H, (int)Nq, (int)D,
+                a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0], a->do_stride[1], a->do_stride[2]);
+        else
+            gae::attn_bwd_delta_kernel<__half><<<blocks, 256, 0, st>>>(
+                (const __half *)a->o, (const __half *)a->dout, delta, (int)B, (int)H, (int)Nq, (int)D,
+                a->o_stride[0], a->o_stride[1], a->o_stride[2], a->do_stride[0], a->do_stride[1], a->do_stride[2]);
+        GAE_CUDA_TRY(cudaGetLastError());
+    }
+    gae::AttnBwdParams p;
+    memset(&p, 0, sizeof(p));
+    const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    gae_status s;
+    if ((s = make_map_4d(&p.tm_q, a->q, dt, 2, B, H, Nq, D, a->q_stride[0], a->q_stride[1], a->q_stride[2], 128)) ||
+        (s = make_map_4d(&p.tm_k, a->k, dt, 2, B, H, Nkv, D, a->k_stride[0], a->k_stride[1], a->k_stride[2], 128)) ||
+        (s = make_map_4d(&p.tm_v, a->v, dt, 2, B, H, Nkv, D, a->v_stride[0], a->v_stride[1], a->v_stride[2], 128)) ||
+        (s = make_map_4d(&p.tm_do, a->dout, dt, 2, B, H, Nq, D, a->do_stride[0], a->do_stride[1], a->do_stride[2],
+                         128)))
+        return s;
+    p.lse = a->lse;
+    p.delta = delta;
+    p.dq_acc = dq_acc;
+    p.dk = a->dk;
+    p.dv = a->dv;
+    p.dk_sb = a->dk_stride[0]; p.dk_sh = a->dk_stride[1]; p.dk_ss = a->dk_stride[2];
+    p.dv_sb = a->dv_stride[0]; p.dv_sh = a->dv_stride[1]; p.dv_ss = a->dv_stride[2];
+    p.B = (int)B; p.H = (int)H; p.Nq = (int)Nq; p.Nkv = (int)Nkv;
+    p.causal = a->causal ? 1 : 0;
+    p.scale = a->scale;
+    p.scale_log2 = a->scale * 1.4426950408889634f;
+    dim3 grid((unsigned)((Nkv + 127) / 128), (unsigned)(B * H));
+    if (D == 128) s = bf16 ? launch_bwd_tc<128, true>(p, grid, st) : launch_bwd_tc<128, false>(p, grid, st);
+    else s = bf16 ? launch_bwd_tc<64, true>(p, grid, st) : launch_bwd_tc<64, false>(p, grid, st);
+    if (s != GAE_OK) return s;
+    {
+        const int64_t total4 = B * H * Nq * D / 4;
+        const unsigned blocks = (unsigned)((total4 + 255) / 256);
+        if (bf16)
+            gae::attn_bwd_dq_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(
+                dq_acc, (__nv_bfloat16 *)a->dq, (int)B, (int)H, (int)Nq, (int)D, a->dq_stride[0], a->dq_stride[1],
+                a->dq_stride[2]);
+        else
+            gae::attn_bwd_dq_kernel<__half><<<blocks, 256, 0, st>>>(dq_acc, (__half *)a->dq, (int)B, (int)H,
+                                                                      (int)Nq, (int)D, a->dq_stride[0],
+                                                                      a->dq_stride[1], a->dq_stride[2]);
+        GAE_CUDA_TRY(cudaGetLastError());
+    }
+    return GAE_OK;
 }
 
 gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st) {
@@ -728,6 +827,17 @@ gae_status gae_layer_stack_fwd(const gae_layer_args *a, const gae_layer_weights 
         cur = nxt;
     }
     return GAE_OK;
+}
+
+size_t gae_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq_q, int64_t head_dim) {
+    if (batch < 1 || heads < 1 || seq_q < 1 || head_dim < 1) return 0;
+    return attn_bwd_ws_region(batch, heads, seq_q, head_dim) +
+           (((size_t)(batch * heads * seq_q) * 4 + 255) & ~(size_t)255);
+}
+
+gae_status gae_attn_bwd(const gae_attn_bwd_args *args, void *stream) {
+    if (!args) return fail(GAE_ERR_INVALID_ARG, "NULL args");
+    return launch_attn_bwd(args, static_cast<cudaStream_t>(stream));
 }
 
 size_t gae_symphony_workspace_bytes(int64_t seq_len, int64_t head_dim) {

@@ -132,6 +132,50 @@ typedef struct {
 GAE_API gae_status gae_attn_fwd(const gae_attn_args *args, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Attention backward: dQ, dK, dV of the exact attention computed by
+ * gae_attn_fwd, from Q, K, V, the forward output O, the output gradient dO
+ * and the forward's LSE (natural log, [batch*heads, seq_q] as gae_attn_fwd
+ * writes it).  No reference counterpart: the reference crate is
+ * inference-only; this is the training-side caller of its operator
+ * (P = softmax(scale * Q K^T), dV = P^T dO, dS = P o (dO V^T - rowsum(dO o O)),
+ * dQ = scale * dS K, dK = scale * dS^T Q).
+ * bf16 or f16, head_dim 64 or 128; causal requires seq_q == seq_kv (the
+ * forward's mask with zero offsets).  Every pointer 16-byte aligned and every
+ * stride a multiple of 8 elements.  `workspace`: device memory of at least
+ * gae_attn_bwd_workspace_bytes(batch, heads, seq_q, head_dim) bytes (fp32 dQ
+ * accumulator and the per-row dO.O sums).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *q;
+    const void *k;
+    const void *v;
+    const void *o;
+    const void *dout;
+    const float *lse;
+    void *dq;
+    void *dk;
+    void *dv;
+    int64_t batch, heads, seq_q, seq_kv, head_dim;
+    int64_t q_stride[3];        /* element strides: batch, head, seq */
+    int64_t k_stride[3];
+    int64_t v_stride[3];
+    int64_t o_stride[3];
+    int64_t do_stride[3];
+    int64_t dq_stride[3];
+    int64_t dk_stride[3];
+    int64_t dv_stride[3];
+    gae_dtype dtype;
+    int causal;
+    float scale;
+    void *workspace;
+    size_t workspace_bytes;
+} gae_attn_bwd_args;
+
+GAE_API size_t gae_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq_q, int64_t head_dim);
+
+GAE_API gae_status gae_attn_bwd(const gae_attn_bwd_args *args, void *stream);
+
+/* ------------------------------------------------------------------------
  * INT8 attention (replaces cuda_src/waller_operator_int8.cu:27-67,
  * waller_operator_int8_tc.cu:38-87, waller_operator_int8_tiled.cu:15-189).
  * q, k: int8 [batch*heads, seq, head_dim] contiguous, with fp32 per-row

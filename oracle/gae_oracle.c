@@ -620,3 +620,64 @@ void ora_symphony_layer(const float *input, const int8_t *k, const int8_t *v, co
         free(state); free(res); free(acc); free(hid); free(q);
     }
 }
+
+/* Attention backward (an extension: the reference is inference-only).  The
+ * standard gradients of O = softmax(scale * Q K^T) V per (batch, head) slice,
+ * computed directly from the definition in double precision:
+ *   P = softmax rows (causal: keys j <= i), dV = P^T dO, dP = dO V^T,
+ *   dS = P o (dP - rowsum(dO o O)) with O recomputed here, dQ = scale dS K,
+ *   dK = scale dS^T Q.
+ * q, dout: [BH, nq, d]; k, v: [BH, nkv, d]; outputs likewise (float). */
+void ora_attention_bwd(const float *q, const float *k, const float *v, const float *dout, size_t BH,
+                       size_t nq, size_t nkv, size_t d, float scale, int causal, float *dq, float *dk,
+                       float *dv) {
+    #pragma omp parallel for schedule(dynamic, 1)
+    for (size_t bh = 0; bh < BH; ++bh) {
+        const float *Q = q + bh * nq * d, *K = k + bh * nkv * d, *V = v + bh * nkv * d;
+        const float *G = dout + bh * nq * d;
+        float *dQ = dq + bh * nq * d, *dK = dk + bh * nkv * d, *dV = dv + bh * nkv * d;
+        double *P = (double *)malloc(nkv * sizeof(double));
+        double *dKa = (double *)calloc(nkv * d, sizeof(double));
+        double *dVa = (double *)calloc(nkv * d, sizeof(double));
+        double *o = (double *)malloc(d * sizeof(double));
+        for (size_t i = 0; i < nq; ++i) {
+            const size_t nk = causal ? (i + 1 < nkv ? i + 1 : nkv) : nkv;
+            double mx = -INFINITY;
+            for (size_t j = 0; j < nk; ++j) {
+                double s = 0.0;
+                for (size_t c = 0; c < d; ++c) s += (double)Q[i * d + c] * (double)K[j * d + c];
+                P[j] = s * scale;
+                if (P[j] > mx) mx = P[j];
+            }
+            double sum = 0.0;
+            for (size_t j = 0; j < nk; ++j) { P[j] = exp(P[j] - mx); sum += P[j]; }
+            for (size_t c = 0; c < d; ++c) o[c] = 0.0;
+            for (size_t j = 0; j < nk; ++j) {
+                P[j] /= sum;
+                for (size_t c = 0; c < d; ++c) o[c] += P[j] * (double)V[j * d + c];
+            }
+            double delta = 0.0;
+            for (size_t c = 0; c < d; ++c) delta += o[c] * (double)G[i * d + c];
+            double *dqa = (double *)calloc(d, sizeof(double));
+            for (size_t j = 0; j < nk; ++j) {
+                double dp = 0.0;
+                for (size_t c = 0; c < d; ++c) {
+                    dp += (double)G[i * d + c] * (double)V[j * d + c];
+                    dVa[j * d + c] += P[j] * (double)G[i * d + c];
+                }
+                const double ds = P[j] * (dp - delta);
+                for (size_t c = 0; c < d; ++c) {
+                    dqa[c] += ds * (double)K[j * d + c];
+                    dKa[j * d + c] += ds * (double)Q[i * d + c];
+                }
+            }
+            for (size_t c = 0; c < d; ++c) dQ[i * d + c] = (float)(dqa[c] * scale);
+            free(dqa);
+        }
+        for (size_t x = 0; x < nkv * d; ++x) {
+            dK[x] = (float)(dKa[x] * scale);
+            dV[x] = (float)dVa[x];
+        }
+        free(P); free(dKa); free(dVa); free(o);
+    }
+}

@@ -314,3 +314,18 @@ def symphony_layer(x, k, v, w_up, w_down, n1, n2, tuning, act=0):
                              _f32(w_up), _f32(w_down), _f32(n1), _f32(n2), n, d,
                              _f32(np.asarray(tuning, np.float32)), int(act), out)
     return out
+
+
+def attention_bwd(q, k, v, dout, scale, causal):
+    """Attention gradients (an extension: the reference is inference-only),
+    double precision from the definition.  q, dout [BH, Nq, D]; k, v
+    [BH, Nkv, D].  Returns (dq, dk, dv) float32."""
+    q, k, v, dout = (_f32(a) for a in (q, k, v, dout))
+    BH, nq, d = q.shape
+    nkv = k.shape[1]
+    dq, dk, dv = np.empty_like(q), np.empty_like(k), np.empty_like(v)
+    L = lib()
+    L.ora_attention_bwd.argtypes = [_f32p, _f32p, _f32p, _f32p, _sz, _sz, _sz, _sz, C.c_float, C.c_int,
+                                    _f32p, _f32p, _f32p]
+    L.ora_attention_bwd(q, k, v, dout, BH, nq, nkv, d, float(scale), int(bool(causal)), dq, dk, dv)
+    return dq, dk, dv

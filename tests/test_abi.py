@@ -120,3 +120,18 @@ def test_symphony_workspace_and_rejections(gae):
     assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 1 << 30, None) == 1
     tf.activation_type = 0
     assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 16, None) == 1
+
+
+def test_attn_bwd_workspace_and_rejections(gae):
+    L = gae.lib()
+    assert L.gae_attn_bwd_workspace_bytes(2, 3, 100, 64) == (2 * 3 * 100 * 64 * 4 + 255) // 256 * 256 + \
+        (2 * 3 * 100 * 4 + 255) // 256 * 256
+    assert L.gae_attn_bwd(None, None) == 1
+    a = gae.AttnBwdArgs()
+    a.batch, a.heads, a.seq_q, a.seq_kv, a.head_dim = 1, 1, 128, 256, 128
+    a.causal = 1
+    assert L.gae_attn_bwd(C.byref(a), None) == 2  # causal with seq_q != seq_kv
+    a.causal, a.head_dim = 0, 96
+    assert L.gae_attn_bwd(C.byref(a), None) == 2
+    a.head_dim, a.dtype = 128, 1  # bf16
+    assert L.gae_attn_bwd(C.byref(a), None) == 1  # NULL pointers

@@ -167,3 +167,19 @@ def test_int8_quantize_and_logits(ora):
     assert np.allclose(q * s[:, None], x, atol=s.max())
     L = ora.int8_logits(q[None], q[None])
     assert np.array_equal(L[0], q.astype(np.int32) @ q.astype(np.int32).T)
+
+
+def test_attention_bwd_oracle_matches_autograd(ora):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(3)
+    for causal, (n, m) in ((True, (37, 37)), (False, (29, 41))):
+        q, g = (rng.standard_normal((2, n, 16)).astype(np.float32) for _ in range(2))
+        k, v = (rng.standard_normal((2, m, 16)).astype(np.float32) for _ in range(2))
+        dq, dk, dv = ora.attention_bwd(q, k, v, g, 0.3, causal)
+        Q, K, V = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (q, k, v))
+        s = Q @ K.transpose(1, 2) * 0.3
+        if causal:
+            s = s.masked_fill(torch.triu(torch.ones(n, m, dtype=torch.bool), 1), float("-inf"))
+        (torch.softmax(s, -1) @ V).backward(torch.tensor(g, dtype=torch.float64))
+        for got, t in ((dq, Q), (dk, K), (dv, V)):
+            assert np.abs(got - t.grad.numpy()).max() < 1e-5
