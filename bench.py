@@ -64,6 +64,9 @@ WORKLOADS = {
     "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
     "gpt2": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-gpt2-small-12L", gpt2=True,
                  layers=12, d_model=768, d_ff=3072),
+    # training-side backward of config 2 causal (no reference counterpart)
+    "mha-bwd": dict(B=4, H=16, N=8192, D=128, causal=True, cfg="config2-causal-backward", bwd=True,
+                    metric="attention backward TFLOPS (bf16 d=128)"),
     # the reference's fused symphony layer (waller_fused_layer.cu:64-247) at its
     # benchmark's largest single-launch length with HEAD_DIM 64 (:17, :407)
     "symphony": dict(B=1, H=1, N=131072, D=64, causal=True, cfg="symphony-layer-131072-d64",
@@ -225,6 +228,18 @@ def cpu_sample(w, slices=8, rows_cap=None):
         flops = 4.0 * D * n_rows * N * slices
         return (flops / dt / 1e12, dt, f"{slices} head(s) x {n_rows} query rows, full key range each",
                 oracle.num_threads())
+    if w.get("bwd"):
+        # gradients of one (batch, head) slice over its first `rows_cap` tokens
+        # (a causal prefix is a complete problem of its own)
+        n = N if rows_cap is None else min(N, rows_cap)
+        q, k, v, g = (rng.standard_normal((slices, n, D)).astype(np.float32) for _ in range(4))
+        oracle.lib()
+        t0 = time.perf_counter()
+        oracle.attention_bwd(q, k, v, g, 1.0 / math.sqrt(D), w["causal"])
+        dt = time.perf_counter() - t0
+        return (2.5 * attn_flops(1, slices, n, n, D, w["causal"]) / dt / 1e12, dt,
+                f"gradients of {slices} slice(s) over the first {n} tokens (float64 oracle)",
+                oracle.num_threads())
     if w.get("sym"):
         # the first `rows_cap` tokens: a causal prefix is a complete layer of its own
         n = N if rows_cap is None else min(N, rows_cap)
@@ -269,6 +284,18 @@ def run_reference(args, w):
         for _ in range(min(args.steps, 5)):
             v, s, desc, threads = cpu_sample(w)
             vals.append(v); secs.append(s)
+        return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
+    if w.get("bwd"):
+        budget = 120.0 / (args.steps + args.warmup)
+        _, s_cal, _, _ = cpu_sample(w, slices=1, rows_cap=512)
+        n = int(min(w["N"], 512 * math.sqrt(budget / max(s_cal, 1e-6))))
+        n = max(256, n // 128 * 128)
+        for _ in range(args.warmup):
+            cpu_sample(w, slices=1, rows_cap=n)
+        vals, secs = [], []
+        for _ in range(args.steps):
+            v_, s_, desc, threads = cpu_sample(w, slices=1, rows_cap=n)
+            vals.append(v_); secs.append(s_)
         return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
     if w.get("sym") and args.reference_kernel:
         return run_reference_kernel(args, w)
@@ -412,7 +439,22 @@ def main():
     is_int8 = bool(w.get("int8"))
     is_gpt2 = bool(w.get("gpt2"))
     is_sym = bool(w.get("sym"))
-    if is_sym:
+    is_bwd = bool(w.get("bwd"))
+    if is_bwd:
+        q0, k, v = make_inputs(torch, w, dev, 1000 + rank)
+        o0, lse0 = gae.attention(q0, k, v, causal=causal, return_lse=True)
+        g = torch.Generator(device="cpu").manual_seed(2000 + rank)
+        do0 = torch.randn(q0.shape, generator=g).to(torch.bfloat16).to(dev)
+        q = (q0, o0, do0, lse0)
+        grads = torch.empty((3,) + tuple(q0.shape), dtype=q0.dtype, device=dev)
+        out = grads
+        bws = torch.empty(gae.lib().gae_attn_bwd_workspace_bytes(B, H, N, D), dtype=torch.uint8, device=dev)
+        flops = 2.5 * attn_flops(B, H, N, N, D, causal)  # S recomputed, dP, dV, dK, dQ
+
+        def run_step(q, k, v):
+            gae.attention_backward(q[0], k, v, q[1], q[2], q[3], causal=causal, dq=grads[0], dk=grads[1],
+                                   dv=grads[2], workspace=bws)
+    elif is_sym:
         arrs = symphony_arrays(N, D, 1000 + rank)
         sd = {n_: torch.from_numpy(a_).to(dev) for n_, a_ in arrs.items()}
         tf = gae.TuningFork.reference_defaults(D)
@@ -513,6 +555,8 @@ def main():
         launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
     if is_sym:
         launches_per_step = 3  # prep, attention, post
+    if is_bwd:
+        launches_per_step = 3  # dO.O row sums, backward, dQ conversion (plus one memset)
 
     # ---- end to end through the public API with host buffers ---------------
     def flat(t):
@@ -528,6 +572,8 @@ def main():
             return ts[0], ts[0], ts[0]
         if is_int8:
             return (ts[0], ts[1]), (ts[2], ts[3]), ts[4]
+        if is_bwd:
+            return (ts[0], ts[1], ts[2], ts[3]), ts[4], ts[5]
         return ts[0], ts[1], ts[2]
 
     # Pipelined end to end: the host->device copy of step i+1 (copy stream)
@@ -597,6 +643,8 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         if is_sym:
             v_cpu, s_cpu, desc, threads = cpu_sample(w, rows_cap=16384)
+        elif is_bwd:
+            v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=1, rows_cap=1024)
         elif w.get("int8"):
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=2, rows_cap=2048)
         else:

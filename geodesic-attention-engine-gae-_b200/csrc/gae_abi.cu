@@ -268,6 +268,20 @@ gae_status launch_attn_bwd(const gae_attn_bwd_args *a, cudaStream_t st) {
         (s = make_map_4d(&p.tm_do, a->dout, dt, 2, B, H, Nq, D, a->do_stride[0], a->do_stride[1], a->do_stride[2],
                          128)))
         return s;
+    {
+        // fp32 dQ accumulator [B*H, Nq, D]: 3-D map so that a tile's rows past
+        // Nq (the ragged end of a head) fall outside the tensor and are skipped.
+        EncodeTiledFn enc = encode_fn();
+        if (!enc) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+        cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)Nq, (cuuint64_t)(B * H)};
+        cuuint64_t strides[2] = {(cuuint64_t)(D * 4), (cuuint64_t)(Nq * D * 4)};
+        cuuint32_t box[3] = {32, 128, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = enc(&p.tm_dq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return fail(GAE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    }
     p.lse = a->lse;
     p.delta = delta;
     p.dq_acc = dq_acc;
