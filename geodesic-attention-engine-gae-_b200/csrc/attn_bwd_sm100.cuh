@@ -152,6 +152,15 @@ __device__ __forceinline__ uint32_t sw128_chunk(int row, int ch) {
     return (uint32_t)((ch >> 3) * (128 * 128) + row * 128 + (((ch & 7) ^ (row & 7)) << 4));
 }
 
+// Every kBwdPolyPeriod-th pair of probabilities is computed by the
+// polynomial exp2 on the FMA pipe instead of the MUFU (0 = never): the P
+// phase issues 16384 exponentials per tile against 16 MUFU results per
+// cycle per SM.
+#ifndef GAE_BWD_EMU_PERIOD
+#define GAE_BWD_EMU_PERIOD 3
+#endif
+constexpr int kBwdPolyPeriod = GAE_BWD_EMU_PERIOD;
+
 template <int D, bool kBF16>
 __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_constant__ AttnBwdParams p) {
     using Cfg = AttnBwdCfg<D>;
@@ -486,15 +495,25 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                 tmem_ld32(tS, r0);
                 tmem_ld32(tS + 32, r1);
                 tmem_wait_ld();
+                const uint64_t sl2x2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-lse2, -lse2);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int k0 = 2 * e;
-                    float p0 = (k0 < lim) ? ex2_approx(__uint_as_float(r0[2 * e]) * p.scale_log2 - lse2) : 0.f;
-                    float p1 = (k0 + 1 < lim) ? ex2_approx(__uint_as_float(r0[2 * e + 1]) * p.scale_log2 - lse2) : 0.f;
+                for (int e = 0; e < 32; ++e) {
+                    const uint32_t *r = (e < 16) ? r0 : r1;
+                    const int ee = e & 15, k0 = 2 * e;
+                    const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[2 * ee]), __uint_as_float(r[2 * ee + 1])),
+                                              sl2x2, nl2);
+                    float p0, p1;
+                    if (kBwdPolyPeriod > 0 && e % kBwdPolyPeriod == kBwdPolyPeriod - 1) {
+                        exp2_poly_x2(x, p0, p1);  // this pair on the FMA pipe
+                    } else {
+                        float x0, x1;
+                        f2_unpack(x, x0, x1);
+                        p0 = ex2_approx(x0);
+                        p1 = ex2_approx(x1);
+                    }
+                    p0 = (k0 < lim) ? p0 : 0.f;
+                    p1 = (k0 + 1 < lim) ? p1 : 0.f;
                     pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
-                    p0 = (k0 + 32 < lim) ? ex2_approx(__uint_as_float(r1[2 * e]) * p.scale_log2 - lse2) : 0.f;
-                    p1 = (k0 + 33 < lim) ? ex2_approx(__uint_as_float(r1[2 * e + 1]) * p.scale_log2 - lse2) : 0.f;
-                    pk[16 + e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }
             }
             // dS_{i-1} stays in the tile until dQ_{i-1}, its last reader, completed.
