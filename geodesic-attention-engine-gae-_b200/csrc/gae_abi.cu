@@ -868,7 +868,6 @@ gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v
     if (!input || !k || !v || !w_up || !w_down || !norm1_w || !norm2_w || !tf || !output || !workspace)
         return fail(GAE_ERR_INVALID_ARG, "NULL pointer in symphony arguments");
     if (n < 0 || (d != 64 && d != 128)) return fail(GAE_ERR_UNSUPPORTED, "symphony supports head_dim 64 or 128");
-    if (tf->activation_type < 0 || tf->activation_type > 2) return fail(GAE_ERR_INVALID_ARG, "activation_type must be 0, 1 or 2");
     if (!(tf->attn_temperature != 0.f)) return fail(GAE_ERR_INVALID_ARG, "attn_temperature is zero");
     const size_t need = gae_symphony_workspace_bytes(n, d);
     if (workspace_bytes < need) return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", workspace_bytes, need);

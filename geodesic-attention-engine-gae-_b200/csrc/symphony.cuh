@@ -36,6 +36,7 @@ __global__ void symphony_prep_kernel(const float *x, const int8_t *k, const int8
     vh[i] = __int2half_rn((int)v[i]);
 }
 
+// waller_fused_layer.cu:35-46; any other type is the identity (its default branch).
 __device__ __forceinline__ float sym_activation(float x, int type) {
     switch (type) {
         case 0: return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));

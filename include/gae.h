@@ -306,7 +306,8 @@ GAE_API gae_status gae_linear_fwd(const void *x, const void *w, const float *bia
  * causal attention with int8 K and the integer values of int8 V,
  * score = dot * attn_scale / attn_temperature; state = x*residual_alpha +
  * attn -> RMSNorm(norm1_w, norm_eps) -> MLP (x @ w_up [d, 4d], activation
- * 0 GELU-tanh / 1 SiLU / 2 ReLU^2, @ w_down [4d, d], * mlp_gate) ->
+ * 0 GELU-tanh / 1 SiLU / 2 ReLU^2 / any other value the identity, as the
+ * reference's `default:` branch, @ w_down [4d, d], * mlp_gate) ->
  * state*residual_beta + mlp -> RMSNorm(norm2_w) -> * output_scale.
  * input/output fp32 [seq_len, head_dim], k/v int8 [seq_len, head_dim], weights
  * fp32 row-major; head_dim 64 or 128; input, output, w_up, w_down and the

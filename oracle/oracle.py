@@ -36,6 +36,19 @@ def build() -> str:
 
 
 REF_SYMPHONY_PATH = os.path.join(_HERE, "_ref", "libref_symphony.so")
+REF_SYMPHONY128_PATH = os.path.join(_HERE, "_ref", "libref_symphony128.so")
+
+
+def ref_symphony128():
+    """ctypes handle on the reference's head_dim-128 fused layer kernel
+    (waller_fused_realistic.cu, built by oracle/ref_symphony_realistic.cu),
+    or None where it was not built.  Same arguments as ref_symphony_fwd."""
+    if not os.path.exists(REF_SYMPHONY128_PATH):
+        return None
+    L = C.CDLL(REF_SYMPHONY128_PATH)
+    vp = C.c_void_p
+    L.ref_symphony128_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, C.c_int, _f32p, C.c_int, vp]
+    return L
 
 
 def ref_symphony():

@@ -116,9 +116,9 @@ def test_symphony_workspace_and_rejections(gae):
                               None, None, 0, None) == 1
     p = 1 << 20
     assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 96, C.byref(tf), p, p, 1 << 30, None) == 2
-    tf.activation_type = 3
+    tf.attn_temperature = 0.0
     assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 1 << 30, None) == 1
-    tf.activation_type = 0
+    tf.attn_temperature = 1.0
     assert L.gae_symphony_fwd(p, p, p, p, p, p, p, 16, 64, C.byref(tf), p, p, 16, None) == 1
 
 

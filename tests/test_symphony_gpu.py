@@ -39,7 +39,7 @@ def _ora_tuning(tf):
 
 
 @pytest.mark.parametrize("d", [64, 128])
-@pytest.mark.parametrize("act", [0, 1, 2])
+@pytest.mark.parametrize("act", [0, 1, 2, 3])
 def test_symphony_matches_oracle(gae, ora, d, act):
     n = 1000
     arrays = _case(n, d, 7 + d + act)
@@ -77,23 +77,30 @@ def test_symphony_rejects_bad_args(gae):
                              workspace=small)
 
 
-def test_reference_kernel_pins_oracle_and_product(gae, ora):
-    """The reference's own waller_fused_symphony_kernel (built from its source
-    into oracle/_ref) on the reference benchmark's input distribution
-    (waller_fused_layer.cu:265-280 style: uniform inputs, small uniform
+@pytest.mark.parametrize("d", [64, 128])
+def test_reference_kernel_pins_oracle_and_product(gae, ora, d):
+    """The reference's own fused-layer kernels, built from its source into
+    oracle/_ref (d=64: waller_fused_symphony_kernel, waller_fused_layer.cu;
+    d=128: waller_fused_128, waller_fused_realistic.cu:26-148), on the
+    reference benchmark's input distribution (uniform inputs, small uniform
     weights, unit norms) against the oracle and against gae_symphony_fwd.
 
-    seq_len is a multiple of the reference's 128-thread block: in a partial
-    last block the reference's exited threads (row >= seq_len, :89) skip their
-    share of the cooperative K/V tile loads (:133-145), so the block's live
-    rows read tile entries that were never written.  Its benchmark lengths are
-    all multiples of 128; this library computes the defined result for every
-    length (test_symphony_matches_oracle runs ragged lengths)."""
-    ref_lib = ora.ref_symphony()
-    if ref_lib is None:
-        pytest.skip("reference symphony kernel not built (no reference tree where build() ran)")
-    n, d = 2048, 64
-    rng = np.random.default_rng(2026)
+    seq_len is a multiple of the reference's thread blocks (128 and 32): in a
+    partial last block the reference's exited threads (row >= seq_len)
+    skip their share of the cooperative K/V tile loads, so the block's live
+    rows read tile entries that were never written.  Its benchmark lengths
+    are all multiples of the block; this library computes the defined result
+    for every length (test_symphony_matches_oracle runs ragged lengths)."""
+    if d == 64:
+        ref_lib = ora.ref_symphony()
+        launch = ref_lib.ref_symphony_fwd if ref_lib is not None else None
+    else:
+        ref_lib = ora.ref_symphony128()
+        launch = ref_lib.ref_symphony128_fwd if ref_lib is not None else None
+    if launch is None:
+        pytest.skip("reference fused-layer kernel not built (no reference tree where build() ran)")
+    n = 2048
+    rng = np.random.default_rng(2026 + d)
     x = (rng.integers(0, 1000, (n, d)) / 1000.0 - 0.5).astype(np.float32)
     k = rng.integers(-128, 128, (n, d)).astype(np.int8)
     v = rng.integers(-128, 128, (n, d)).astype(np.int8)
@@ -101,22 +108,23 @@ def test_reference_kernel_pins_oracle_and_product(gae, ora):
     w_down = (rng.integers(0, 1000, (4 * d, d)) / 10000.0 - 0.05).astype(np.float32)
     n1 = np.ones(d, np.float32)
     n2 = np.ones(d, np.float32)
-    for act in (0, 1, 2):
+    # waller_fused_realistic.cu's activation has no ReLU^2 case: its type 2
+    # falls through to the identity (:17-23), which is type 3 here and in
+    # waller_fused_layer.cu.
+    for act in (0, 1, 2, 3):
         tf = gae.TuningFork.reference_defaults(d)
-        tf.activation_type = act
+        tf.activation_type = act if d == 64 or act != 2 else 3
         tfa = np.asarray(_ora_tuning(tf), np.float32)
         dev = {name: torch.from_numpy(a).cuda() for name, a in
                dict(x=x, k=k, v=v, w_up=w_up, w_down=w_down, n1=n1, n2=n2).items()}
         out_ref = torch.empty_like(dev["x"])
         st = torch.cuda.current_stream().cuda_stream
-        assert ref_lib.ref_symphony_fwd(dev["k"].data_ptr(), dev["v"].data_ptr(),
-                                        dev["w_up"].data_ptr(), dev["w_down"].data_ptr(),
-                                        dev["n1"].data_ptr(), dev["n2"].data_ptr(),
-                                        dev["x"].data_ptr(), out_ref.data_ptr(), n, tfa, act,
-                                        st) == 0
+        assert launch(dev["k"].data_ptr(), dev["v"].data_ptr(), dev["w_up"].data_ptr(),
+                      dev["w_down"].data_ptr(), dev["n1"].data_ptr(), dev["n2"].data_ptr(),
+                      dev["x"].data_ptr(), out_ref.data_ptr(), n, tfa, act, st) == 0
         torch.cuda.synchronize()
         ref_gpu = out_ref.cpu().numpy()
-        oracle_out = ora.symphony_layer(x, k, v, w_up, w_down, n1, n2, tfa, act)
+        oracle_out = ora.symphony_layer(x, k, v, w_up, w_down, n1, n2, tfa, tf.activation_type)
         # oracle vs the reference kernel: same op order, fp32 throughout; only
         # expf/tanhf/rsqrtf ulps and the reference's FMA contraction differ.
         assert float(np.abs(oracle_out - ref_gpu).max()) <= 1e-3
