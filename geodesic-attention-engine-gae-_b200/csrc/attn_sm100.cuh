@@ -186,7 +186,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     // every role advances identically.
     const int BH = p.B * p.H;
     const int n_units = p.n_qpairs * BH;
-    struct Unit { int q0, b, h, bh, n_kv; };
+    // skip0: under the causal mask the unit's last K/V tile lies wholly above
+    // the diagonal of Q tile 0, so group 0 runs one tile fewer than group 1.
+    struct Unit { int q0, b, h, bh, n_kv, skip0; };
     auto unit_at = [&](int u) {
         Unit x;
         // head-major keeps the K/V of a head in L2 while its query blocks run
@@ -203,6 +205,11 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             n = (last_key < 0) ? 0 : (int)min64((int64_t)n, last_key / Cfg::kBlockN + 1);
         }
         x.n_kv = n;
+        x.skip0 = 0;
+        if (p.causal && n >= 2) {
+            const int64_t last_q0 = p.q_offset + (int64_t)min(x.q0 + 127, p.Nq - 1);
+            x.skip0 = (p.kv_offset + (int64_t)(n - 1) * Cfg::kBlockN > last_q0) ? 1 : 0;
+        }
         return x;
     };
     // Serpentine assignment: in round k this CTA takes list entry
@@ -334,8 +341,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             };
             bool ok = true;
             int ib = 0;  // ring item of this unit's K_0
-            int gt = 0;  // running tile (phase of s_full / p_full)
-            int au = 0;  // running active unit (phase of q_full / q_empty / o_full)
+            int gt0 = 0, gt1 = 0;  // running tiles of groups 0 / 1 (phase of s_full / p_full)
+            int au = 0;            // running active unit (phase of q_full / q_empty / o_full)
             for (int k = 0; k * G < n_units && ok; ++k) {
                 const int u = unit_of(k);
                 if (u >= n_units) continue;
@@ -350,17 +357,19 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     if (!ok) break;
                     if (j > 0) {
                         ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                             mbar_wait(bar_p(0), (gt + j - 1) & 1, kSiteP, abort_flag);
+                             mbar_wait(bar_p(0), (gt0 + j - 1) & 1, kSiteP, abort_flag);
                         if (!ok) break;
                         if (au == 0) GAE_TRACE(kTrMmaP0, j - 1);
                         tc_fence_after();
                         issue_pv(0, v_slot, j - 1 > 0);
                     }
-                    issue_qk(0, k_slot);
-                    umma_commit(bar_s(0));
+                    if (!(x.skip0 && j == n_kv - 1)) {
+                        issue_qk(0, k_slot);
+                        umma_commit(bar_s(0));
+                    }
                     if (au == 0) GAE_TRACE(kTrMmaIssued0, j);
                     if (j > 0) {
-                        ok = mbar_wait(bar_p(1), (gt + j - 1) & 1, kSiteP, abort_flag);
+                        ok = mbar_wait(bar_p(1), (gt1 + j - 1) & 1, kSiteP, abort_flag);
                         if (!ok) break;
                         if (au == 0) GAE_TRACE(kTrMmaP1, j - 1);
                         tc_fence_after();
@@ -377,20 +386,25 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 }
                 if (!ok) break;
                 const int v_item = ib + 2 * n_kv - 1, v_slot = v_item % Cfg::kStages;
-                ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                     mbar_wait(bar_p(0), (gt + n_kv - 1) & 1, kSiteP, abort_flag);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(0, v_slot, n_kv > 1);
-                umma_commit(bar_o(0));
-                if (!(ok = mbar_wait(bar_p(1), (gt + n_kv - 1) & 1, kSiteP, abort_flag))) break;
+                if (!(ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag)))
+                    break;
+                if (x.skip0) {
+                    umma_commit(bar_o(0));  // PV0 of its last tile was issued in the loop
+                } else {
+                    if (!(ok = mbar_wait(bar_p(0), (gt0 + n_kv - 1) & 1, kSiteP, abort_flag))) break;
+                    tc_fence_after();
+                    issue_pv(0, v_slot, n_kv > 1);
+                    umma_commit(bar_o(0));
+                }
+                if (!(ok = mbar_wait(bar_p(1), (gt1 + n_kv - 1) & 1, kSiteP, abort_flag))) break;
                 tc_fence_after();
                 issue_pv(1, v_slot, n_kv > 1);
                 umma_commit(bar_o(1));
                 umma_commit(bar_kv_empty(v_slot));
                 if (Cfg::kInt8) mbar_arrive(bar_kv_empty((v_item - 1) % Cfg::kStages));
                 ib += 2 * n_kv;
-                gt += n_kv;
+                gt0 += n_kv - x.skip0;
+                gt1 += n_kv;
                 ++au;
             }
             // Drain: every MMA this thread issued has completed before TMEM is
@@ -414,6 +428,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 if (u >= n_units) continue;
         const Unit x = unit_at(u);
         const int n_kv = x.n_kv, b = x.b, h = x.h, bh = x.bh;
+        const int n_mine = n_kv - (grp == 0 ? x.skip0 : 0);  // K/V tiles this group processes
         const int q_local = x.q0 + grp * 128 + row;
         const int64_t q_abs = p.q_offset + q_local;
         // Factor that takes a raw score to the log2 domain: scale*log2(e), times
@@ -428,7 +443,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
 
         float m_run = -INFINITY;  // exponent base, log2 domain (scaled)
         float l_run = 0.f;
-        for (int j = 0; j < n_kv; ++j) {
+        for (int j = 0; j < n_mine; ++j) {
             ok = mbar_wait(bar_s(grp), (gt + j) & 1, kSiteS, abort_flag);
             if (!ok) break;
             if (row == 0 && au == 0) GAE_TRACE(kTrSWait0 + grp, j);
@@ -595,7 +610,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         }
         if (n_kv > 0) {
             ib += 2 * n_kv;
-            gt += n_kv;
+            gt += n_mine;
             ++au;
         }
         }  // units

@@ -187,8 +187,19 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     // gain most from keeping TMEM, barriers and the K/V stream alive, measured
     // +20%).  head_dim 128: one CTA per unit, balanced by the hardware's block
     // scheduler (equal or better under the power cap, measured).
-    const bool persistent = D == 64 && units > num_sms();
+    bool persistent = D == 64 && units > num_sms();
     p.head_major = persistent ? 0 : 1;
+    {
+        // Diagnostics overrides of the schedule: GAE_ATTN_PERSISTENT=0/1 and
+        // GAE_ATTN_HEAD_MAJOR=0/1 (unit order of the persistent grid).
+        static const char *env_p = getenv("GAE_ATTN_PERSISTENT");
+        static const char *env_h = getenv("GAE_ATTN_HEAD_MAJOR");
+        if (env_p && (env_p[0] == '0' || env_p[0] == '1')) {
+            persistent = env_p[0] == '1' && units > num_sms();
+            p.head_major = persistent ? 0 : 1;
+        }
+        if (persistent && env_h && (env_h[0] == '0' || env_h[0] == '1')) p.head_major = env_h[0] - '0';
+    }
     dim3 grid((unsigned)(persistent ? num_sms() : units));
 
     if (D == 128) {
