@@ -64,6 +64,9 @@ constexpr int kTraceTiles = 256;
 enum TraceEvent : int {
     kTrSWait0 = 0, kTrSWait1, kTrPDone0, kTrPDone1,  // softmax group g: S ready / P written
     kTrMmaP0, kTrMmaP1, kTrMmaIssued0, kTrMmaIssued1,  // MMA warp: P_g seen / MMAs issued
+    // per active unit (index = the CTA's unit count): CTA set up (unit 0
+    // only), group 0 saw its first S, group 0 epilogue start / end
+    kTrCtaStart, kTrUnitFirstS, kTrEpiStart, kTrEpiEnd,
     kTrNumEvents
 };
 __device__ unsigned long long *gae_attn_trace = nullptr;
@@ -110,11 +113,15 @@ struct AttnCfg {
     static constexpr int kKScaleBytes = kInt8 ? kBlockN * 4 : 0;  // per-key scales after K
     static constexpr int kSlotBytes = kVTileBytes;               // >= K tile + its scales
     static constexpr int kStages = (D == 128) ? (kInt8 ? 5 : 4) : 8;  // K/V ring slots
-    static constexpr int kQBytes = 2 * kQTileBytes;
+    static constexpr int kQBytes = 2 * kQTileBytes;  // one unit's two Q tiles
+    // Q buffers: at head_dim 64 (persistent grid, short units) the next unit's
+    // Q loads while the current one runs; at 128 shared memory allows one.
+    static constexpr int kQStages = (D == 64) ? 2 : 1;
     static constexpr int kRingBytes = kStages * kSlotBytes;
-    static constexpr int kBarOffset = kQBytes + kRingBytes;
-    // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done, q_empty
-    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1;  // + q_empty
+    static constexpr int kBarOffset = kQStages * kQBytes + kRingBytes;
+    // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done, q_empty,
+    // q_full / q_empty of the second Q stage
+    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 2;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
@@ -157,17 +164,17 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     const uint32_t base = (raw_addr + 1023u) & ~1023u;
     uint8_t *smem = smem_raw + (base - raw_addr);
 
-    const uint32_t sQ = base;
-    const uint32_t sRing = base + Cfg::kQBytes;
+    auto sQ = [&](int st) { return base + st * Cfg::kQBytes; };
+    const uint32_t sRing = base + Cfg::kQStages * Cfg::kQBytes;
     const uint32_t sBar = base + Cfg::kBarOffset;
-    auto bar_q = [&]() { return sBar; };
+    auto bar_q = [&](int st) { return st ? sBar + 8u * (9 + 2 * Cfg::kStages) : sBar; };
     auto bar_kv_full = [&](int s) { return sBar + 8u * (1 + s); };
     auto bar_kv_empty = [&](int s) { return sBar + 8u * (1 + Cfg::kStages + s); };
     auto bar_s = [&](int i) { return sBar + 8u * (1 + 2 * Cfg::kStages + i); };
     auto bar_p = [&](int i) { return sBar + 8u * (3 + 2 * Cfg::kStages + i); };
     auto bar_o = [&](int i) { return sBar + 8u * (5 + 2 * Cfg::kStages + i); };
     const uint32_t bar_done = sBar + 8u * (7 + 2 * Cfg::kStages);
-    const uint32_t bar_q_empty = sBar + 8u * (8 + 2 * Cfg::kStages);
+    auto bar_q_empty = [&](int st) { return sBar + 8u * (st ? 10 + 2 * Cfg::kStages : 8 + 2 * Cfg::kStages); };
     uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kBarOffset + Cfg::kNumBars * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
@@ -223,8 +230,10 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         if (unit_of(k) < n_units) any_work = unit_at(unit_of(k)).n_kv > 0;
 
     if (threadIdx.x == 0) {
-        mbar_init(bar_q(), 1);
-        mbar_init(bar_q_empty, 1);
+        for (int st = 0; st < 2; ++st) {
+            mbar_init(bar_q(st), 1);
+            mbar_init(bar_q_empty(st), 1);
+        }
         for (int s = 0; s < Cfg::kStages; ++s) {
             mbar_init(bar_kv_full(s), 1);
             mbar_init(bar_kv_empty(s), 1);
@@ -246,6 +255,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = any_work ? *tmem_base_slot : 0u;
+    if (threadIdx.x == 0) GAE_TRACE(kTrCtaStart, 0);
 
     if (warp >= 10) {
         regs_dec<Cfg::kRegsProducer>();
@@ -286,14 +296,15 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 const Unit x = unit_at(u);
                 if (x.n_kv == 0) continue;
                 // K_0, V_0 first: they only need free ring slots, while Q waits
-                // for the previous unit's last QK^T.
+                // for the last QK^T of the unit that used its stage before.
                 for (int it = 0; it < 2 && ok; ++it) load_item(x, 0, it);
                 if (!ok) break;
-                if (au > 0 && !(ok = mbar_wait(bar_q_empty, (au - 1) & 1, kSiteQ, abort_flag))) break;
-                mbar_expect_tx(bar_q(), Cfg::kQBytes);
+                const int qs = au % Cfg::kQStages, qu = au / Cfg::kQStages;  // stage, its use
+                if (qu > 0 && !(ok = mbar_wait(bar_q_empty(qs), (qu - 1) & 1, kSiteQ, abort_flag))) break;
+                mbar_expect_tx(bar_q(qs), Cfg::kQBytes);
                 for (int t = 0; t < 2; ++t)
                     for (int hf = 0; hf < Cfg::kQKBoxes; ++hf)
-                        tma_load_4d(sQ + t * Cfg::kQTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(),
+                        tma_load_4d(sQ(qs) + t * Cfg::kQTileBytes + hf * Cfg::kBoxBytes, &p.tm_q, bar_q(qs),
                                     hf * 128 / (Cfg::kInt8 ? 1 : 2), x.q0 + t * 128, x.h, x.b);
                 for (int j = 1; j < x.n_kv && ok; ++j)
                     for (int kv = 0; kv < 2 && ok; ++kv) load_item(x, j, kv);
@@ -301,7 +312,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             }
             // Drain: the last Q and the last copy issued into each slot have
             // landed before the CTA can exit (bounded; normally complete).
-            if (au > 0) mbar_wait(bar_q(), (au - 1) & 1, kSiteQ, &no_abort);
+            for (int a = max(0, au - Cfg::kQStages); a < au; ++a)
+                mbar_wait(bar_q(a % Cfg::kQStages), (a / Cfg::kQStages) & 1, kSiteQ, &no_abort);
             for (int i = max(0, item - Cfg::kStages); i < item; ++i)
                 mbar_wait(bar_kv_full(i % Cfg::kStages), (i / Cfg::kStages) & 1, kSiteKvFull, &no_abort);
         }
@@ -312,9 +324,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             constexpr uint32_t idesc_qk =
                 Cfg::kInt8 ? idesc_i8(128, 128) : idesc_f16(128, 128, kBF16, false, false);
             constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, false, true);
-            auto issue_qk = [&](int i, int slot) {
+            auto issue_qk = [&](int i, int slot, uint32_t q_base) {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
-                const uint32_t qa = sQ + i * Cfg::kQTileBytes;
+                const uint32_t qa = q_base + i * Cfg::kQTileBytes;
                 const uint32_t kb = sRing + slot * Cfg::kSlotBytes;
                 // One MMA consumes 32 bytes of K (16 bf16 or 32 int8 elements).
 #pragma unroll
@@ -342,6 +354,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             bool ok = true;
             int ib = 0;  // ring item of this unit's K_0
             int gt0 = 0, gt1 = 0;  // running tiles of groups 0 / 1 (phase of s_full / p_full)
+            bool early_qk0 = false;  // this unit's QK0 of tile 0 was issued during the previous unit
             int au = 0;            // running active unit (phase of q_full / q_empty / o_full)
             for (int k = 0; k * G < n_units && ok; ++k) {
                 const int u = unit_of(k);
@@ -349,7 +362,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 const Unit x = unit_at(u);
                 const int n_kv = x.n_kv;
                 if (n_kv == 0) continue;
-                if (!(ok = mbar_wait(bar_q(), au & 1, kSiteQ, abort_flag))) break;
+                const int qs = au % Cfg::kQStages;
+                const uint32_t q_base = sQ(qs);
+                if (!(ok = mbar_wait(bar_q(qs), (au / Cfg::kQStages) & 1, kSiteQ, abort_flag))) break;
                 for (int j = 0; j < n_kv && ok; ++j) {
                     const int k_item = ib + 2 * j, k_slot = k_item % Cfg::kStages;
                     const int v_item = ib + 2 * j - 1, v_slot = v_item % Cfg::kStages;
@@ -363,8 +378,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                         tc_fence_after();
                         issue_pv(0, v_slot, j - 1 > 0);
                     }
-                    if (!(x.skip0 && j == n_kv - 1)) {
-                        issue_qk(0, k_slot);
+                    if (!(x.skip0 && j == n_kv - 1) && !(early_qk0 && j == 0)) {
+                        issue_qk(0, k_slot, q_base);
                         umma_commit(bar_s(0));
                     }
                     if (au == 0) GAE_TRACE(kTrMmaIssued0, j);
@@ -378,10 +393,10 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                         // int8: both softmax groups have read K_{j-1}'s scales from its slot.
                         if (Cfg::kInt8) mbar_arrive(bar_kv_empty((k_item - 2) % Cfg::kStages));
                     }
-                    issue_qk(1, k_slot);
+                    issue_qk(1, k_slot, q_base);
                     umma_commit(bar_s(1));
                     if (!Cfg::kInt8) umma_commit(bar_kv_empty(k_slot));
-                    if (j == n_kv - 1) umma_commit(bar_q_empty);  // Q may be reloaded after this
+                    if (j == n_kv - 1) umma_commit(bar_q_empty(qs));  // Q may be reloaded after this
                     if (au == 0) GAE_TRACE(kTrMmaIssued1, j);
                 }
                 if (!ok) break;
@@ -395,6 +410,26 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     tc_fence_after();
                     issue_pv(0, v_slot, n_kv > 1);
                     umma_commit(bar_o(0));
+                }
+                // Group 0 is done with this unit while group 1 still works on its
+                // last tile: if the next unit's Q and K_0 have landed, start its
+                // first QK0 now (S0 was released with group 0's last P; tcgen05
+                // MMAs of this thread run in issue order, so the PV0 above reads
+                // it first).  Only probes, so group 1's last tile never waits.
+                early_qk0 = false;
+                for (int k2 = k + 1; k2 * G < n_units; ++k2) {
+                    const int u2 = unit_of(k2);
+                    if (u2 >= n_units || unit_at(u2).n_kv == 0) continue;
+                    const int qs2 = (au + 1) % Cfg::kQStages;
+                    const int k2_item = ib + 2 * n_kv, k2_slot = k2_item % Cfg::kStages;
+                    if (mbar_test(bar_q(qs2), ((au + 1) / Cfg::kQStages) & 1) &&
+                        mbar_test(bar_kv_full(k2_slot), (k2_item / Cfg::kStages) & 1)) {
+                        tc_fence_after();
+                        issue_qk(0, k2_slot, sQ(qs2));
+                        umma_commit(bar_s(0));
+                        early_qk0 = true;
+                    }
+                    break;
                 }
                 if (!(ok = mbar_wait(bar_p(1), (gt1 + n_kv - 1) & 1, kSiteP, abort_flag))) break;
                 tc_fence_after();
@@ -447,6 +482,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             ok = mbar_wait(bar_s(grp), (gt + j) & 1, kSiteS, abort_flag);
             if (!ok) break;
             if (row == 0 && au == 0) GAE_TRACE(kTrSWait0 + grp, j);
+            if (row == 0 && grp == 0 && j == 0) GAE_TRACE(kTrUnitFirstS, au);
             tc_fence_after();
             float s[128];
             {
@@ -467,7 +503,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                         break;
                     }
                     const float4 *ks = reinterpret_cast<const float4 *>(
-                        smem + Cfg::kQBytes + slot * Cfg::kSlotBytes + Cfg::kKTileBytes);
+                        smem + Cfg::kQStages * Cfg::kQBytes + slot * Cfg::kSlotBytes + Cfg::kKTileBytes);
 #pragma unroll
                     for (int e4 = 0; e4 < 8; ++e4) {
                         const float4 a = ks[e4], bq = ks[8 + e4], c = ks[16 + e4], d = ks[24 + e4];
@@ -574,6 +610,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         // Epilogue: O_i / l -> global; log-sum-exp.
         const bool row_valid = q_local < p.Nq;
         const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
+        if (row == 0 && grp == 0) GAE_TRACE(kTrEpiStart, au);
         if (n_kv > 0 && ok) ok = mbar_wait(bar_o(grp), au & 1, kSiteO, abort_flag);
         if (n_kv > 0 && ok) {
             tc_fence_after();
@@ -603,6 +640,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                          2 * (b * p.o_sb + h * p.o_sh + (int64_t)q_local * p.o_ss);
             for (int c = 0; c < D / 8; ++c) reinterpret_cast<uint4 *>(orow)[c] = make_uint4(0, 0, 0, 0);
         }
+        if (row == 0 && grp == 0) GAE_TRACE(kTrEpiEnd, au);
         if (p.lse && row_valid) {
             float lse = -INFINITY;
             if (l_run > 0.f) lse = (m_run + __log2f(l_run)) * 0.69314718055994531f;

@@ -23,8 +23,9 @@ extern "C" {
  * buf[event * GAE_TRACE_TILES + tile] (unsigned 64-bit, device memory of
  * GAE_TRACE_EVENTS * GAE_TRACE_TILES entries).  Events: 0/1 softmax group
  * 0/1 saw S, 2/3 group 0/1 published P, 4/5 MMA warp saw P of group 0/1,
- * 6/7 MMA warp issued group 0/1's MMAs for that tile, 8/9 group 0/1 has
- * S in registers, 10/11 group 0/1 has its row max.  CTA index x counts
+ * 6/7 MMA warp issued group 0/1's MMAs for that tile (these per K/V tile
+ * of the CTA's first unit); per unit of the CTA: 8 CTA set up (unit 0),
+ * 9 group 0 saw the unit's first S, 10/11 group 0 epilogue start / end.  CTA index x counts
  * from the heaviest query block (x = 0 is the last 256 query rows). */
 GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
 
