@@ -19,7 +19,7 @@
 //   dV += P^T dO                (P from shared memory read MN-major)
 //   dK += dS^T Q                (dS likewise)
 //   dQ  = dS K                  (dS K-major, K MN-major) into dP's columns
-// in the order  dV_i, S_{i+1}, dK_i, dQ_i, then dP_{i+1} (two 64-column
+// in the order  dV_i, S_{i+1}, dQ_i, dK_i, then dP_{i+1} (two 64-column
 // halves, each as soon as the drain has read that half of dQ_i) and dV_{i+1}
 // in whichever order their inputs become ready.  S_{i+1} runs while the
 // compute warps turn dP_i into dS_i, and they find it ready when they start
@@ -32,8 +32,8 @@
 // sum, and draining it stays off the compute warps' path.
 //
 // Reuse of the P/dS tile: dS_i overwrites P_i only after the dV_i MMA that
-// reads P_i has completed; P_{i+1} overwrites dS_i only after dQ_i (issued
-// after dK_i; tcgen05 MMAs of one thread complete in order) has completed.
+// reads P_i has completed; P_{i+1} overwrites dS_i only after dK_i (issued
+// after dQ_i; tcgen05 MMAs of one thread complete in order) has completed.
 //
 // Warps: 0-7 compute (two warpgroups; thread = row of the 128-row tile and
 // one half of its columns), 8-11 dQ drain, 12 TMA, 13 MMA (owns TMEM),
@@ -94,8 +94,9 @@ struct AttnBwdCfg {
     static constexpr int kOffK = 0, kOffV = kTile, kOffQ = 2 * kTile, kOffDO = 4 * kTile;
     static constexpr int kOffPS = 5 * kTile, kOffDQ = kOffPS + kPTile, kOffBar = kOffDQ + kHalfBoxes * kBox;
     // kv, q_full[2], q_empty[2], do_full, do_empty, s, dp, p, p_consumed, ds, dq, dq_free[2], done,
+    // ds_consumed,
     // staging_full, staging_free
-    static constexpr int kNumBars = 18;
+    static constexpr int kNumBars = 19;
     static constexpr int kPayload = kOffBar + kNumBars * 8 + 16;
     // + slack for aligning the base to 1024 bytes (the swizzle atoms); the
     // kernel checks at run time that the aligned payload fits.
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
     const uint32_t bar_s = sBar + 56, bar_dp = sBar + 64, bar_p = sBar + 72, bar_pc = sBar + 80;
     const uint32_t bar_ds = sBar + 88, bar_dq = sBar + 96, bar_done = sBar + 104;
     const uint32_t bar_st_full = sBar + 112, bar_st_free = sBar + 120;
+    const uint32_t bar_dsc = sBar + 144;  // after dq_free[2]
     auto bar_dq_free = [&](int hh) { return sBar + 128u + 8u * hh; };  // half hh of dQ read from TMEM
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kOffBar + Cfg::kNumBars * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -214,6 +216,7 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
         mbar_init(bar_pc, 1);
         mbar_init(bar_ds, 256);
         mbar_init(bar_dq, 1);
+        mbar_init(bar_dsc, 1);
         mbar_init(bar_dq_free(0), 128);
         mbar_init(bar_dq_free(1), 128);
         mbar_init(bar_done, 1);
@@ -336,12 +339,8 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                 if (!(ok = mbar_wait(bar_ds, ph, kSiteBwdDS, abort_flag))) break;
                 GAE_TRACE(kBtMmaDS, it);
                 tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_f16_ss(tmem + Cfg::kColDK, smem_desc_sw128(sPS + kk * 2048, Cfg::kBox, 1024),
-                                smem_desc_sw128(sQ(st) + kk * 2048, Cfg::kBox, 1024), id_t, (it > 0 || kk > 0));
-                umma_commit(bar_q_empty(st));
-                // dQ = dS K: M = queries, K = keys (K-major in dS), N = D (MN-major in K).
+                // dQ = dS K first (its drain gates dP_{i+1}): M = queries, K = keys
+                // (K-major in dS), N = D (MN-major in K).
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t off = (kk >> 2) * Cfg::kBox + (kk & 3) * 32;
@@ -349,6 +348,12 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                                 smem_desc_sw128(sK + kk * 2048, Cfg::kBox, 1024), id_dq, kk > 0);
                 }
                 umma_commit(bar_dq);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    umma_f16_ss(tmem + Cfg::kColDK, smem_desc_sw128(sPS + kk * 2048, Cfg::kBox, 1024),
+                                smem_desc_sw128(sQ(st) + kk * 2048, Cfg::kBox, 1024), id_t, (it > 0 || kk > 0));
+                umma_commit(bar_q_empty(st));
+                umma_commit(bar_dsc);  // dS_i's last reader done: the tile may take P_{i+1}
                 if (it + 1 < n_it) {
                     // dP_{i+1} (per half, once the drain has read that half of dQ_i
                     // and dO_{i+1} has landed) and dV_{i+1} (once P_{i+1} is in the
@@ -516,8 +521,8 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                     pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }
             }
-            // dS_{i-1} stays in the tile until dQ_{i-1}, its last reader, completed.
-            if (it > 0 && !(ok = mbar_wait(bar_dq, (it - 1) & 1, kSiteBwdDQ, abort_flag))) break;
+            // dS_{i-1} stays in the tile until dK_{i-1}, its last reader, completed.
+            if (it > 0 && !(ok = mbar_wait(bar_dsc, (it - 1) & 1, kSiteBwdDQ, abort_flag))) break;
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 st_shared_v4(sPS + sw128_chunk(row, 8 * g + c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
