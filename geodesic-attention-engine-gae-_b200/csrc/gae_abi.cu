@@ -685,14 +685,8 @@ gae_status launch_symphony_post(const float *x, const __half *attn, const float 
                                       const float *w_down, const float *n1, const float *n2, int64_t n,
                                       const gae::SymTuning &t, float *out, cudaStream_t st) {
     using P = gae::SymPost<D>;
-    static bool configured[64] = {};
-    int dev = 0;
-    GAE_CUDA_TRY(cudaGetDevice(&dev));
-    if (dev < 64 && !configured[dev]) {
-        GAE_CUDA_TRY(cudaFuncSetAttribute(gae::symphony_post_kernel<D>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P::kSmem));
-        configured[dev] = true;
-    }
+    gae_status s = set_smem(gae::symphony_post_kernel<D>, (int)P::kSmem);
+    if (s != GAE_OK) return s;
     const unsigned blocks = (unsigned)((n + P::T - 1) / P::T);
     gae::symphony_post_kernel<D><<<blocks, P::kThreads, P::kSmem, st>>>(x, attn, w_up, w_down, n1, n2, n, t, out);
     GAE_CUDA_TRY(cudaGetLastError());
