@@ -135,3 +135,32 @@ def test_attn_bwd_workspace_and_rejections(gae):
     assert L.gae_attn_bwd(C.byref(a), None) == 2
     a.head_dim, a.dtype = 128, 1  # bf16
     assert L.gae_attn_bwd(C.byref(a), None) == 1  # NULL pointers
+
+
+_STRUCTS = [("gae_attn_args", "AttnArgs"), ("gae_attn_bwd_args", "AttnBwdArgs"),
+            ("gae_attn_int8_args", "AttnInt8Args"), ("gae_layer_args", "LayerArgs"),
+            ("gae_layer_weights", "LayerWeights"), ("gae_tuning_fork", "TuningFork")]
+
+
+def test_ctypes_mirrors_match_the_header(gae, tmp_path):
+    """Every ctypes mirror in the package has the C struct's size and field
+    offsets, as the C compiler lays out include/gae.h."""
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "gae.h"', "int main(void) {"]
+    for cname, pyname in _STRUCTS:
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in getattr(gae, pyname)._fields_:
+            lines.append(f'printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.splitlines():
+        cname, key, val = line.split()
+        got[(cname, key)] = int(val)
+    for cname, pyname in _STRUCTS:
+        cls = getattr(gae, pyname)
+        assert C.sizeof(cls) == got[(cname, "size")], cname
+        for field, _ in cls._fields_:
+            assert getattr(cls, field).offset == got[(cname, field)], (cname, field)
