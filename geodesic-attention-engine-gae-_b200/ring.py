@@ -195,3 +195,96 @@ def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "
         out = _redeal(out, r, P, group, False)
         lse = _redeal(lse.unsqueeze(-1), r, P, group, False).squeeze(-1)
     return (out, lse) if return_lse else out
+
+
+def _default_attend_bwd(q, k, v, out, dout, lse, causal, scale):
+    from . import attention_backward
+    return attention_backward(q, k, v, out, dout, lse, causal=causal, scale=scale)
+
+
+def ring_attention_backward(q, k, v, out, dout, lse, *, group=None, causal: bool = True,
+                            balance: str = "zigzag", scale: float | None = None, attend_bwd=None):
+    """Gradients (dq, dk, dv) of ring_attention for this rank's shards.
+
+    q, k, v, dout: this rank's contiguous shards [B, H, S, D]; out and lse:
+    this rank's output and log-sum-exp from ring_attention(return_lse=True)
+    with the same group, causal and balance.  Each block pair goes through
+    the library's backward kernel (gae_attn_bwd) with the final output and
+    LSE of the query rows, which makes the per-pair gradients exact parts of
+    the full ones: dq sums over the K/V blocks this rank meets, and each K/V
+    block carries fp32 dK/dV accumulators around the ring with it, handed on
+    after every step and returned to the block's owner after the last one.
+    """
+    attend_bwd = attend_bwd or _default_attend_bwd
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
+    B, H, S, D = q.shape
+    for t in (k, v, out, dout):
+        if t.shape != q.shape:
+            raise ValueError("ring_attention_backward: q, k, v, out, dout shards must have the same shape")
+    if lse.shape != (B, H, S):
+        raise ValueError("ring_attention_backward: lse must be [B, H, S]")
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    zig = causal and balance == "zigzag"
+    if zig and S % 2:
+        raise ValueError("ring_attention_backward: zig-zag balance needs an even shard length")
+    if balance not in ("zigzag", "contiguous"):
+        raise ValueError(f"unknown balance {balance!r}")
+
+    if zig:
+        C = S // 2
+        if P > 1:
+            q, k, v, out, dout = (_redeal(t, r, P, group, True) for t in (q, k, v, out, dout))
+            lse = _redeal(lse.unsqueeze(-1), r, P, group, True).squeeze(-1)
+        chunks_of = lambda rank: [(rank, 0, C), (2 * P - 1 - rank, C, C)]
+    else:
+        C = S
+        chunks_of = lambda rank: [(rank, 0, S)]
+
+    kv = torch.stack([k, v])
+    kv_next = torch.empty_like(kv) if P > 1 else None
+    dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)  # travels with kv
+    dkv_next = torch.empty_like(dkv) if P > 1 else None
+    dq = torch.zeros(q.shape, dtype=torch.float32, device=q.device)
+
+    for t in range(P):
+        src = (r - t) % P
+        reqs = []
+        if t < P - 1:  # the next K/V block travels while this one is used
+            try:
+                reqs = dist.batch_isend_irecv([dist.P2POp(dist.isend, kv, (r + 1) % P, group),
+                                               dist.P2POp(dist.irecv, kv_next, (r - 1) % P, group)])
+            except Exception as e:
+                raise _comm_error(f"posting the K/V exchange of backward step {t}", e) from e
+        for qc, qo, ql in chunks_of(r):
+            qs = slice(qo, qo + ql)
+            lse_c = lse[:, :, qs].contiguous()
+            for kc, ko, kl in chunks_of(src):
+                if causal and kc > qc:
+                    continue  # every key after every query: no gradient
+                ks = slice(ko, ko + kl)
+                dq_p, dk_p, dv_p = attend_bwd(q[:, :, qs], kv[0][:, :, ks], kv[1][:, :, ks],
+                                              out[:, :, qs], dout[:, :, qs], lse_c,
+                                              causal and kc == qc, scale)
+                dq[:, :, qs] += dq_p.float()
+                dkv[0][:, :, ks] += dk_p.float()
+                dkv[1][:, :, ks] += dv_p.float()
+        try:
+            for w in reqs:
+                w.wait()
+        except Exception as e:
+            raise _comm_error(f"the K/V exchange of backward step {t}", e) from e
+        if P > 1:
+            # Hand this block's accumulators on with it (after the last step
+            # they reach the block's owner).
+            _exchange([dist.P2POp(dist.isend, dkv, (r + 1) % P, group),
+                       dist.P2POp(dist.irecv, dkv_next, (r - 1) % P, group)],
+                      f"the dK/dV exchange of backward step {t}")
+            dkv, dkv_next = dkv_next, dkv
+            if t < P - 1:
+                kv, kv_next = kv_next, kv
+
+    dq, dk, dv = dq.to(q.dtype), dkv[0].to(q.dtype), dkv[1].to(q.dtype)
+    if zig and P > 1:
+        dq, dk, dv = (_redeal(t, r, P, group, False) for t in (dq, dk, dv))
+    return dq, dk, dv

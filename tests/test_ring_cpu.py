@@ -88,3 +88,57 @@ def test_zigzag_owner_is_a_balanced_partition():
         for r in range(P):
             mine = [c for c in range(2 * P) if owners[c] == r]
             assert mine == [r, 2 * P - 1 - r]
+
+
+def _block_bwd(q, k, v, out, dout, lse, causal, scale):
+    """One block pair's share of the gradients given the final output and LSE
+    of its query rows (what gae_attn_bwd computes), in float64."""
+    q, k, v, out, dout, lse = (t.double() for t in (q, k, v, out, dout, lse))
+    s = q @ k.transpose(-1, -2) * scale
+    if causal:
+        n, m = s.shape[-2:]
+        s = s.masked_fill(torch.triu(torch.ones(n, m, dtype=torch.bool), 1), float("-inf"))
+    p = torch.exp(s - lse.unsqueeze(-1))
+    dv = p.transpose(-1, -2) @ dout
+    dp = dout @ v.transpose(-1, -2)
+    ds = p * (dp - (dout * out).sum(-1, keepdim=True))
+    return ds @ k * scale, ds.transpose(-1, -2) @ q * scale, dv
+
+
+def _bwd_worker(rank, world, port, causal, balance, result_dir):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import __graft_entry__ as ge
+    ge.load_package()
+    from gae_b200 import ring
+    B, H, S, D = 1, 2, 8, 16
+    g = torch.Generator().manual_seed(43)
+    full = [torch.randn(B, H, S * world, D, generator=g) for _ in range(4)]
+    q, k, v, do = (t[:, :, rank * S:(rank + 1) * S].contiguous() for t in full)
+    o, lse = ring.ring_attention(q, k, v, causal=causal, balance=balance, return_lse=True,
+                                 attend=_oracle_attend, merge=_oracle_merge)
+    dq, dk, dv = ring.ring_attention_backward(q, k, v, o, do, lse, causal=causal, balance=balance,
+                                              attend_bwd=_block_bwd)
+    for name, t in (("dq", dq), ("dk", dk), ("dv", dv)):
+        np.save(os.path.join(result_dir, f"{name}{rank}.npy"), t.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("causal,balance", [(True, "zigzag"), (True, "contiguous"),
+                                            (False, "contiguous")])
+def test_ring_backward_matches_full_gradients(tmp_path, ora, world, causal, balance):
+    port = _free_port()
+    mp.spawn(_bwd_worker, args=(world, port, causal, balance, str(tmp_path)), nprocs=world,
+             join=True)
+    B, H, S, D = 1, 2, 8, 16
+    g = torch.Generator().manual_seed(43)
+    full = [torch.randn(B, H, S * world, D, generator=g) for _ in range(4)]
+    f = lambda t: t.numpy().reshape(B * H, S * world, D)
+    refs = ora.attention_bwd(f(full[0]), f(full[1]), f(full[2]), f(full[3]), 1 / math.sqrt(D), causal)
+    for name, ref in zip(("dq", "dk", "dv"), refs):
+        got = np.concatenate([np.load(tmp_path / f"{name}{r}.npy") for r in range(world)], axis=2)
+        assert np.abs(got.reshape(ref.shape) - ref).max() < 1e-4, name

@@ -35,6 +35,26 @@ def test_ring_single_gpu(gae, ora, causal, balance):
     assert float(np.abs(lse.cpu().numpy() - rlse).max()) <= 1e-3
 
 
+@pytest.mark.parametrize("causal,balance", [(True, "zigzag"), (False, "contiguous")])
+def test_ring_backward_single_gpu(gae, ora, causal, balance):
+    """P=1 ring backward (zig-zag: three block pairs, two of them causal
+    diagonals) through gae_attn_bwd, against the oracle's full gradients.
+    Tolerance: max abs error <= 2e-2 of each gradient's largest value."""
+    from gae_b200 import ring
+    B, H, N, D = 1, 2, 512, 128
+    q, k, v = _inputs(B, H, N, D)
+    do = _inputs(B, H, N, D, seed=9)[0]
+    qd, kd, vd, dod = (t.cuda() for t in (q, k, v, do))
+    o, lse = ring.ring_attention(qd, kd, vd, causal=causal, balance=balance, return_lse=True)
+    grads = ring.ring_attention_backward(qd, kd, vd, o, dod, lse, causal=causal, balance=balance)
+    torch.cuda.synchronize()
+    gae.device_status()
+    f = lambda t: t.float().cpu().numpy().reshape(B * H, N, D)
+    refs = ora.attention_bwd(f(q), f(k), f(v), f(do), 1 / math.sqrt(D), causal)
+    for got, ref in zip(grads, refs):
+        assert float(np.abs(f(got) - ref).max() / np.abs(ref).max()) <= 2e-2
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -56,10 +76,14 @@ def _nccl_worker(rank, world, port, out_dir):
     q, k, v = _inputs(B, H, N, D)
     S = N // world
     sl = slice(rank * S, (rank + 1) * S)
-    o = ring.ring_attention(q[:, :, sl].cuda(), k[:, :, sl].cuda(), v[:, :, sl].cuda(),
-                            causal=True)
+    do = _inputs(B, H, N, D, seed=9)[0]
+    qs, ks, vs, dos = (t[:, :, sl].cuda() for t in (q, k, v, do))
+    o, lse = ring.ring_attention(qs, ks, vs, causal=True, return_lse=True)
+    grads = ring.ring_attention_backward(qs, ks, vs, o, dos, lse, causal=True)
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"o{rank}.npy"), o.float().cpu().numpy())
+    for name, t in zip(("dq", "dk", "dv"), grads):
+        np.save(os.path.join(out_dir, f"{name}{rank}.npy"), t.float().cpu().numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -77,3 +101,9 @@ def test_ring_multi_gpu(ora, tmp_path):
                                 1 / math.sqrt(D), True)
     got = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=2)
     assert float(np.abs(got - ref).max()) <= 2e-2
+    do = _inputs(B, H, N, D, seed=9)[0]
+    f = lambda t: t.float().numpy().reshape(B * H, N, D)
+    refs = ora.attention_bwd(f(q), f(k), f(v), f(do), 1 / math.sqrt(D), True)
+    for name, r in zip(("dq", "dk", "dv"), refs):
+        g = np.concatenate([np.load(tmp_path / f"{name}{i}.npy") for i in range(world)], axis=2)
+        assert float(np.abs(g.reshape(r.shape) - r).max() / np.abs(r).max()) <= 2e-2, name
