@@ -206,3 +206,24 @@ def test_quantize_rows_int8_bit_exact(gae, ora):
     q, s = gae.quantize_rows_int8(xb.cuda())
     rq, rs = ora.quantize_rows_int8(xb.float().numpy())
     assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_tc_scores_growing_along_keys(gae, ora, D, causal):
+    """Keys whose scores grow along the sequence, so that a row's running max
+    keeps rising by more than the lazy rescale's headroom from tile to tile:
+    exercises the rebasing and the recomputation after a speculative tile."""
+    B, H, N = 1, 2, 1024
+    g = torch.Generator().manual_seed(21)
+    q = torch.randn(B, H, N, D, generator=g).abs()
+    k = torch.randn(B, H, N, D, generator=g).abs() * torch.linspace(0.1, 3.0, N).view(1, 1, N, 1)
+    v = torch.randn(B, H, N, D, generator=g)
+    q, k, v = (t.bfloat16() for t in (q, k, v))
+    o, lse = gae.attention(q.cuda(), k.cuda(), v.cuda(), causal=causal, return_lse=True)
+    torch.cuda.synchronize()
+    gae.device_status()
+    ref, rlse = ora.attention_batched(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                      1 / math.sqrt(D), causal, want_lse=True)
+    assert float(np.abs(o.float().cpu().numpy() - ref).max()) <= BF16_TOL
+    assert float(np.abs(lse.cpu().numpy() - rlse).max()) <= 1e-3 * max(1.0, float(np.abs(rlse).max()))
