@@ -678,6 +678,66 @@ def layer_stack_forward(layers, x, out=None, workspace=None, stream=None):
     return out
 
 
+def _dev_f32(a, shape=None, dtype=None):
+    torch = _torch()
+    t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+    if shape is not None:
+        t = t.reshape(shape)
+    t = t.to("cuda")
+    return t.to(dtype) if dtype is not None else t
+
+
+def layernorm_batched(input, gamma, beta, batch_size: int, hidden_dim: int, eps: float):
+    """ate::layernorm_batched (rust_src/src/layernorm.rs:20-47) on the GPU
+    LayerNorm kernel: host f32 slices in, host f32 out; rows staged in bf16
+    (hidden_dim % 8 == 0, <= 4096)."""
+    torch = _torch()
+    n = batch_size * hidden_dim
+    x = _dev_f32(_host_f32(input, n)[:n], (batch_size, hidden_dim), torch.bfloat16)
+    y = layernorm_rows(x, _dev_f32(_host_f32(gamma, hidden_dim)[:hidden_dim]),
+                       _dev_f32(_host_f32(beta, hidden_dim)[:hidden_dim]), eps)
+    return y.float().cpu().numpy().reshape(-1)
+
+
+def layernorm(input, gamma, beta, eps: float):
+    """ate::layernorm (layernorm.rs:6-17): one row."""
+    d = len(gamma)
+    return layernorm_batched(input, gamma, beta, 1, d, eps)
+
+
+def _mlp_device(x, w1, b1, w2, b2, hidden, mlp, res=None):
+    torch = _torch()
+    # The crate stores W1 [hidden, mlp] and W2 [mlp, hidden] (input-major);
+    # the tensor-core GEMM takes W[out, in].
+    w1d = _dev_f32(np.asarray(w1, np.float32).reshape(hidden, mlp).T, None, torch.bfloat16).contiguous()
+    w2d = _dev_f32(np.asarray(w2, np.float32).reshape(mlp, hidden).T, None, torch.bfloat16).contiguous()
+    hid = linear(x, w1d, bias=_dev_f32(b1), gelu=True)
+    return linear(hid, w2d, bias=_dev_f32(b2), res=res)
+
+
+def mlp_block(input, w1, b1, w2, b2, hidden_dim: int, mlp_dim: int):
+    """ate::mlp_block (rust_src/src/mlp.rs:7-36): gelu(x @ W1 + b1) @ W2 + b2
+    on the tcgen05 GEMM with fused bias / tanh-GELU epilogues.  `input` may
+    hold several tokens (len = tokens * hidden_dim; the crate takes one);
+    hidden_dim and mlp_dim multiples of 256, bf16 activations."""
+    torch = _torch()
+    x = np.asarray(input, np.float32).reshape(-1, hidden_dim)
+    y = _mlp_device(_dev_f32(x, None, torch.bfloat16), w1, b1, w2, b2, hidden_dim, mlp_dim)
+    return y.float().cpu().numpy().reshape(-1)
+
+
+def fused_mlp_layernorm(input, residual, w1, b1, w2, b2, gamma, beta, hidden_dim: int,
+                        mlp_dim: int, eps: float):
+    """ate::fused_mlp_layernorm (mlp.rs:39-73): LayerNorm(mlp_block(x) +
+    residual); the residual add is fused into the second GEMM's epilogue."""
+    torch = _torch()
+    x = _dev_f32(np.asarray(input, np.float32).reshape(-1, hidden_dim), None, torch.bfloat16)
+    r = _dev_f32(np.asarray(residual, np.float32).reshape(-1, hidden_dim), None, torch.bfloat16)
+    y = _mlp_device(x, w1, b1, w2, b2, hidden_dim, mlp_dim, res=r)
+    out = layernorm_rows(y, _dev_f32(gamma), _dev_f32(beta), eps)
+    return out.float().cpu().numpy().reshape(-1)
+
+
 class TransformerBlock:
     """ate::TransformerBlock (rust_src/src/transformer.rs:36-120) on the GPU
     kernels.  Weights keep the crate's layouts (wq/wk/wv/wo [h, h] as

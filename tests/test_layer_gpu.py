@@ -144,3 +144,33 @@ def test_transformer_block_demo_forward(gae, ora):
     nb = gae.TransformerBlock.new_random(cfg)
     out = nb.forward(np.full(n * h, 0.1, np.float32), n)
     assert out.shape == (n * h,) and np.all(np.isfinite(out))
+
+
+def test_crate_layer_primitives(gae, ora):
+    """ate::layernorm / layernorm_batched / mlp_block / fused_mlp_layernorm
+    (layernorm.rs, mlp.rs) on the GPU kernels against the oracle's
+    restatement of the crate; bf16 activations, so the layer tolerance
+    |gpu - ref| <= 5e-2 * max(1, |ref|) (up to four bf16 roundings)."""
+    rng = np.random.default_rng(4)
+    h, m, t = 256, 512, 3
+    x = rng.standard_normal(t * h).astype(np.float32)
+    r = rng.standard_normal(t * h).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(h)).astype(np.float32)
+    w1 = (rng.standard_normal(h * m) * 0.05).astype(np.float32)
+    b1 = (0.1 * rng.standard_normal(m)).astype(np.float32)
+    w2 = (rng.standard_normal(m * h) * 0.05).astype(np.float32)
+    b2 = (0.1 * rng.standard_normal(h)).astype(np.float32)
+    assert within(gae.layernorm(x[:h], g, b, 1e-5), ora.layernorm(x[:h], g, b, 1e-5), 5e-2) <= 5e-2
+    assert within(gae.layernorm_batched(x, g, b, t, h, 1e-5),
+                  ora.layernorm_batched(x, g, b, t, h, 1e-5), 5e-2) <= 5e-2
+    for i in range(t):  # the crate's functions take one token
+        sl = slice(i * h, (i + 1) * h)
+        assert within(gae.mlp_block(x[sl], w1, b1, w2, b2, h, m),
+                      ora.mlp_block(x[sl], w1, b1, w2, b2, h, m), 5e-2) <= 5e-2
+        assert within(gae.fused_mlp_layernorm(x[sl], r[sl], w1, b1, w2, b2, g, b, h, m, 1e-5),
+                      ora.fused_mlp_layernorm(x[sl], r[sl], w1, b1, w2, b2, g, b, h, m, 1e-5),
+                      5e-2) <= 5e-2
+    # several tokens at once give the same rows as one at a time
+    many = gae.mlp_block(x, w1, b1, w2, b2, h, m)
+    assert within(many[:h], ora.mlp_block(x[:h], w1, b1, w2, b2, h, m), 5e-2) <= 5e-2
