@@ -392,6 +392,23 @@ def standard_attention(q, k, v, seq_len: int, head_dim: int, scale: float, causa
 
 
 # ------------------------------------------ scalar helpers of the crate
+class AteGpu:
+    """ate::gpu::AteGpu (rust_src/src/gpu/wgpu_backend.rs:17-146): the crate's
+    GPU backend API, served by this library's CUDA path instead of wgpu.  Its
+    WGSL kernel (gpu/waller.wgsl) is the causal Waller recurrence over
+    [seq_len, head_dim] f32 with the running max starting at -FLT_MAX;
+    waller_operator here runs the fp32 kernel with the reference's operation
+    order (the shader's head_dim <= 64 register array is not a limit here)."""
+
+    @classmethod
+    def new(cls):
+        lib()  # the library loads (and fails loudly) at construction, as wgpu's adapter request would
+        return cls()
+
+    def waller_operator(self, q, k, v, seq_len: int, head_dim: int, scale: float):
+        return waller_operator(q, k, v, seq_len, head_dim, scale, causal=True)
+
+
 class OnlineSoftmax:
     """ate::OnlineSoftmax (rust_src/src/online_softmax.rs:5-41)."""
 

@@ -227,3 +227,14 @@ def test_tc_scores_growing_along_keys(gae, ora, D, causal):
                                       1 / math.sqrt(D), causal, want_lse=True)
     assert float(np.abs(o.float().cpu().numpy() - ref).max()) <= BF16_TOL
     assert float(np.abs(lse.cpu().numpy() - rlse).max()) <= 1e-3 * max(1.0, float(np.abs(rlse).max()))
+
+
+def test_ate_gpu_backend_api(gae, ora):
+    """ate::gpu::AteGpu::{new, waller_operator} (the crate's wgpu backend API)
+    on the CUDA fp32 path: causal, same tolerance as the fp32 path."""
+    rng = np.random.default_rng(17)
+    n, d = 300, 64
+    q, k, v = (rng.standard_normal(n * d).astype(np.float32) for _ in range(3))
+    out = gae.AteGpu.new().waller_operator(q, k, v, n, d, 1 / math.sqrt(d)).reshape(n, d)
+    ref = ora.waller_operator(q, k, v, n, d, 1 / math.sqrt(d), causal=True).reshape(n, d)
+    assert rel_scale(out, ref) <= 1e-5
