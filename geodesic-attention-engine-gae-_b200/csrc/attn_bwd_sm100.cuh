@@ -13,37 +13,32 @@
 // One CTA per (128-key tile j, batch*head): K_j and V_j stay in shared
 // memory, dK_j and dV_j accumulate in TMEM across the CTA's query tiles
 // (causal: tiles i >= j only).  Q_i streams through a two-stage ring, dO_i
-// through one buffer that is reloaded as soon as dP_i and dV_i have read it.
-// The tile is computed transposed, keys on the TMEM lanes, so that P and dS
-// feed the two key-side GEMMs straight from TMEM.  Per query tile the MMA
-// warp issues
-//   S^T  = K Q^T,  dP^T = V dO^T   (K-major x K-major)
-//   dV  += P^T dO                  (P^T from TMEM, dO MN-major)
-//   dK  += dS^T Q                  (dS^T from TMEM, Q MN-major)
-//   dQ   = dS K                    (dS from shared memory read MN-major, K
-//                                   MN-major) into dP^T's columns
-// in the order  dV_i, S^T_{i+1}, dK_i, dQ_i, then dP^T_{i+1} (two 64-query
+// through one buffer that is reloaded as soon as dV_i has read it.  Per
+// query tile the MMA warp issues
+//   S = Q K^T, dP = dO V^T      (K-major x K-major)
+//   dV += P^T dO                (P from shared memory read MN-major)
+//   dK += dS^T Q                (dS likewise)
+//   dQ  = dS K                  (dS K-major, K MN-major) into dP's columns
+// in the order  dV_i, S_{i+1}, dK_i, dQ_i, then dP_{i+1} (two 64-column
 // halves, each as soon as the drain has read that half of dQ_i) and dV_{i+1}
-// in whichever order their inputs become ready.  Two compute warpgroups
-// (thread = key row, one half of the query columns) turn S^T into P^T and
-// dP^T into dS^T, written back over their own fp32 columns as 16-bit pairs;
-// dS is also stored (rows = keys, 128-byte swizzle) for the dQ GEMM.  The
-// per-query LSE and Delta of the next tile are staged in shared memory (two
-// buffers).  A third warpgroup drains dQ_i from TMEM into a swizzled fp32
-// staging box (128 x 32) and a reduce warp adds each box to an fp32
-// accumulator in global memory with TMA reduce-adds
-// (cp.reduce.async.bulk.tensor): query tiles are shared by every key tile, so
-// dQ is the one cross-CTA sum, and draining it stays off the compute path.
+// in whichever order their inputs become ready.  S_{i+1} runs while the
+// compute warps turn dP_i into dS_i, and they find it ready when they start
+// P_{i+1}.  Two compute warpgroups turn S into P and dP into dS (bf16/f16
+// into one shared tile in the 128-byte-swizzled layout both read directions
+// share); a third warpgroup drains dQ_i from TMEM into a swizzled fp32
+// staging tile (two halves) and adds it to an fp32 accumulator in global
+// memory with TMA reduce-adds (cp.reduce.async.bulk.tensor, one per 128 x 32
+// box): query tiles are shared by every key tile, so dQ is the one cross-CTA
+// sum, and draining it stays off the compute warps' path.
 //
-// Ordering that the reuse relies on (tcgen05 MMAs of one thread execute in
-// issue order): S^T_{i+1} overwrites P^T_i after dV_i, which reads it, was
-// issued; dQ_i overwrites dS^T_i after dK_i was issued; dP^T_{i+1} and the dS
-// tile of step i+1 follow the drain of dQ_i, which follows dQ_i's completion.
+// Reuse of the P/dS tile: dS_i overwrites P_i only after the dV_i MMA that
+// reads P_i has completed; P_{i+1} overwrites dS_i only after dQ_i (issued
+// after dK_i; tcgen05 MMAs of one thread complete in order) has completed.
 //
-// Warps: 0-7 compute, 8-11 dQ drain, 12 TMA, 13 MMA (owns TMEM), 14 issues
-// the dQ reduce-adds.  TMEM columns: S^T / P^T [0,128), dP^T / dS^T / dQ
-// [128,256), dV [256,256+D), dK after it; P^T and dS^T of query half g sit in
-// the first 32 columns of that half's 64.
+// Warps: 0-7 compute (two warpgroups; thread = row of the 128-row tile and
+// one half of its columns), 8-11 dQ drain, 12 TMA, 13 MMA (owns TMEM),
+// 14 issues the dQ reduce-adds (so the drain warps never wait on them).
+// TMEM columns: S [0,128), dP / dQ [128,256), dV [256,256+D), dK after it.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -93,15 +88,14 @@ struct AttnBwdCfg {
     static constexpr int kPanels = D * 2 / 128;  // 64-element panels in a 128 x D tile
     static constexpr int kTile = kPanels * kBox;
     static constexpr int kPTile = 2 * kBox;      // 128 x 128, 16-bit
-    static constexpr int kHalfD = D / 2;         // dQ is read from TMEM in two halves
-    static constexpr int kDQBoxes = D / 32;      // fp32 boxes of 128 rows x 32 columns per dQ tile
-    // K, V, Q[2], dO, dS, fp32 dQ staging box, LSE/Delta of two query tiles
+    static constexpr int kHalfD = D / 2;         // dQ is staged and drained in two halves
+    static constexpr int kHalfBoxes = kHalfD / 32;  // fp32 boxes of 128 rows x 32 columns per half
+    // K, V, Q[2], dO, P/dS, fp32 dQ staging (one half)
     static constexpr int kOffK = 0, kOffV = kTile, kOffQ = 2 * kTile, kOffDO = 4 * kTile;
-    static constexpr int kOffPS = 5 * kTile, kOffDQ = kOffPS + kPTile, kOffStats = kOffDQ + kBox;
-    static constexpr int kOffBar = kOffStats + 2 * 2 * 128 * 4;
-    // kv, q_full[2], q_empty[2], do_full, do_empty, s, dp, p, (unused), ds, dq, done,
-    // staging_full, staging_free, dq_free[2], (unused), stats[2]
-    static constexpr int kNumBars = 21;
+    static constexpr int kOffPS = 5 * kTile, kOffDQ = kOffPS + kPTile, kOffBar = kOffDQ + kHalfBoxes * kBox;
+    // kv, q_full[2], q_empty[2], do_full, do_empty, s, dp, p, p_consumed, ds, dq, dq_free[2], done,
+    // staging_full, staging_free
+    static constexpr int kNumBars = 18;
     static constexpr int kPayload = kOffBar + kNumBars * 8 + 16;
     // + slack for aligning the base to 1024 bytes (the swizzle atoms); the
     // kernel checks at run time that the aligned payload fits.
@@ -187,11 +181,9 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
     auto bar_q_full = [&](int st) { return sBar + 8u * (1 + st); };
     auto bar_q_empty = [&](int st) { return sBar + 8u * (3 + st); };
     const uint32_t bar_do_full = sBar + 40, bar_do_empty = sBar + 48;
-    const uint32_t bar_s = sBar + 56, bar_dp = sBar + 64, bar_p = sBar + 72;
+    const uint32_t bar_s = sBar + 56, bar_dp = sBar + 64, bar_p = sBar + 72, bar_pc = sBar + 80;
     const uint32_t bar_ds = sBar + 88, bar_dq = sBar + 96, bar_done = sBar + 104;
     const uint32_t bar_st_full = sBar + 112, bar_st_free = sBar + 120;
-    auto bar_stats = [&](int b) { return sBar + 152u + 8u * b; };  // LSE/Delta buffer b filled
-    float *stats = reinterpret_cast<float *>(smem + Cfg::kOffStats);   // [buffer][lse2 | delta][128]
     auto bar_dq_free = [&](int hh) { return sBar + 128u + 8u * hh; };  // half hh of dQ read from TMEM
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kOffBar + Cfg::kNumBars * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -219,10 +211,9 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
         mbar_init(bar_s, 1);
         mbar_init(bar_dp, 1);
         mbar_init(bar_p, 256);
+        mbar_init(bar_pc, 1);
         mbar_init(bar_ds, 256);
         mbar_init(bar_dq, 1);
-        mbar_init(bar_stats(0), 256);
-        mbar_init(bar_stats(1), 256);
         mbar_init(bar_dq_free(0), 128);
         mbar_init(bar_dq_free(1), 128);
         mbar_init(bar_done, 1);
@@ -280,10 +271,8 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
         if (lane == 0 && n_it > 0) {
             constexpr uint32_t id_qk = idesc_f16(128, 128, kBF16, false, false);
             constexpr uint32_t id_qk_half = idesc_f16(128, 64, kBF16, false, false);
-            constexpr uint32_t id_ts = idesc_f16(128, D, kBF16, false, true);  // P^T dO, dS^T Q (A in TMEM)
-            constexpr uint32_t id_dq = idesc_f16(128, D, kBF16, true, true);   // dS K (A MN-major)
-            // TMEM column of the 16 queries of K-step kk in a packed P^T / dS^T.
-            auto pcol = [](int kk) { return (uint32_t)(kk < 4 ? kk * 8 : 64 + (kk - 4) * 8); };
+            constexpr uint32_t id_t = idesc_f16(128, D, kBF16, true, true);    // P^T dO, dS^T Q
+            constexpr uint32_t id_dq = idesc_f16(128, D, kBF16, false, true);  // dS K
             // 128 x 128 product over the head dimension, both operands K-major.
             auto mma_kk = [&](uint32_t d, uint32_t a, uint32_t bm) {
 #pragma unroll
@@ -297,28 +286,29 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                       mbar_wait(bar_q_full(0), 0, kSiteBwdQFull, abort_flag);
             if (ok) {
                 tc_fence_after();
-                mma_kk(tmem + Cfg::kColS, sK, sQ(0));
+                mma_kk(tmem + Cfg::kColS, sQ(0), sK);
                 umma_commit(bar_s);
                 if ((ok = mbar_wait(bar_do_full, 0, kSiteBwdQFull, abort_flag))) {
                     tc_fence_after();
-                    mma_kk(tmem + Cfg::kColDP, sV, sDO);
+                    mma_kk(tmem + Cfg::kColDP, sDO, sV);
                     umma_commit(bar_dp);
                 }
             }
-            // dV_i += P^T dO: A = P^T from TMEM (M = keys, K = queries), B = dO MN-major.
+            // dV_i: M = keys (MN-major in P), K = queries, N = D.
             auto issue_dv = [&](int it) {
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_f16_ts(tmem + Cfg::kColDV, tmem + Cfg::kColS + pcol(kk),
-                                smem_desc_sw128(sDO + kk * 2048, Cfg::kBox, 1024), id_ts, (it > 0 || kk > 0));
+                    umma_f16_ss(tmem + Cfg::kColDV, smem_desc_sw128(sPS + kk * 2048, Cfg::kBox, 1024),
+                                smem_desc_sw128(sDO + kk * 2048, Cfg::kBox, 1024), id_t, (it > 0 || kk > 0));
+                umma_commit(bar_pc);
             };
-            // Half hh of dP^T = V dO^T: queries [64hh, 64hh + 64) into 64 columns.
+            // Half hh of dP = dO V^T: keys [64hh, 64hh + 64) into 64 columns.
             auto issue_dp_half = [&](int hh) {
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk) {
                     const uint32_t off = (kk >> 2) * Cfg::kBox + (kk & 3) * 32;
-                    umma_f16_ss(tmem + Cfg::kColDP + 64 * hh, smem_desc_sw128(sV + off, 16, 1024),
-                                smem_desc_sw128(sDO + hh * 64 * 128 + off, 16, 1024), id_qk_half, kk > 0);
+                    umma_f16_ss(tmem + Cfg::kColDP + 64 * hh, smem_desc_sw128(sDO + off, 16, 1024),
+                                smem_desc_sw128(sV + hh * 64 * 128 + off, 16, 1024), id_qk_half, kk > 0);
                 }
             };
             bool dv_issued = false;  // dV of the current tile already issued
@@ -340,25 +330,24 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                     if (!(ok = mbar_wait(bar_q_full(sn), ((it + 1) >> 1) & 1, kSiteBwdQFull, abort_flag))) break;
                     GAE_TRACE(kBtMmaS, it + 1);
                     tc_fence_after();
-                    mma_kk(tmem + Cfg::kColS, sK, sQ(sn));
+                    mma_kk(tmem + Cfg::kColS, sQ(sn), sK);
                     umma_commit(bar_s);
                 }
                 if (!(ok = mbar_wait(bar_ds, ph, kSiteBwdDS, abort_flag))) break;
                 GAE_TRACE(kBtMmaDS, it);
                 tc_fence_after();
-                // dK_i += dS^T Q: A = dS^T from TMEM, B = Q MN-major.
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    umma_f16_ts(tmem + Cfg::kColDK, tmem + Cfg::kColDP + pcol(kk),
-                                smem_desc_sw128(sQ(st) + kk * 2048, Cfg::kBox, 1024), id_ts, (it > 0 || kk > 0));
+                    umma_f16_ss(tmem + Cfg::kColDK, smem_desc_sw128(sPS + kk * 2048, Cfg::kBox, 1024),
+                                smem_desc_sw128(sQ(st) + kk * 2048, Cfg::kBox, 1024), id_t, (it > 0 || kk > 0));
                 umma_commit(bar_q_empty(st));
-                // dQ_i = dS K over dS^T's columns (issued after dK_i, which reads
-                // them): A = dS from shared memory (rows = keys: M = queries
-                // contiguous, MN-major), B = K MN-major.
+                // dQ = dS K: M = queries, K = keys (K-major in dS), N = D (MN-major in K).
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    umma_f16_ss(tmem + Cfg::kColDQ, smem_desc_sw128(sPS + kk * 2048, Cfg::kBox, 1024),
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * Cfg::kBox + (kk & 3) * 32;
+                    umma_f16_ss(tmem + Cfg::kColDQ, smem_desc_sw128(sPS + off, 16, 1024),
                                 smem_desc_sw128(sK + kk * 2048, Cfg::kBox, 1024), id_dq, kk > 0);
+                }
                 umma_commit(bar_dq);
                 if (it + 1 < n_it) {
                     // dP_{i+1} (per half, once the drain has read that half of dQ_i
@@ -416,12 +405,13 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
         // ------------------------------------------- dQ reduce-add issuer
         if (lane == 0) {
             bool ok = true;
-            for (int n = 0; n < Cfg::kDQBoxes * n_it && ok; ++n) {
-                const int it = n / Cfg::kDQBoxes, bx = n % Cfg::kDQBoxes;
+            for (int n = 0; n < 2 * n_it && ok; ++n) {
+                const int it = n >> 1, hh = n & 1;
                 if (!(ok = mbar_wait(bar_st_full, n & 1, kSiteBwdDQ, abort_flag))) break;
-                tma_reduce_add_3d(&p.tm_dq, sDQ, bx * 32, (i0 + it) * 128, bh);
+                for (int c = 0; c < Cfg::kHalfBoxes; ++c)
+                    tma_reduce_add_3d(&p.tm_dq, sDQ + c * Cfg::kBox, hh * kHalfD + c * 32, (i0 + it) * 128, bh);
                 bulk_commit();
-                bulk_wait_read();  // the staging box may be rewritten
+                bulk_wait_read();  // the staging tile may be rewritten
                 mbar_arrive(bar_st_free);
             }
             bulk_wait_all();
@@ -436,22 +426,22 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
             if (row == 0) GAE_TRACE(kBtDQ, it);
             tc_fence_after();
             for (int hh = 0; hh < 2 && ok; ++hh) {
+                const int n = 2 * it + hh;  // staging use
                 uint32_t r[kHalfD];
 #pragma unroll
                 for (int c = 0; c < kHalfD / 32; ++c)
                     tmem_ld32(tDQ + hh * kHalfD + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
                 tmem_wait_ld();
                 tc_fence_before();
-                mbar_arrive(bar_dq_free(hh));  // this half of dP^T's columns may be rewritten
+                mbar_arrive(bar_dq_free(hh));  // this half of dP's columns may be rewritten
                 if (row == 0 && hh == 1) GAE_TRACE(kBtDQDone, it);
+                // The previous half's reduce-add has read the staging tile.
+                if (n > 0 && !(ok = mbar_wait(bar_st_free, (n - 1) & 1, kSiteBwdDQFree, abort_flag))) break;
+                // scale * dQ -> staging boxes (128 rows x 32 fp32, 128-byte swizzle:
+                // conflict-free 16-byte stores).
 #pragma unroll
                 for (int c = 0; c < kHalfD / 32; ++c) {
-                    const int n = it * Cfg::kDQBoxes + hh * (kHalfD / 32) + c;  // staging use
-                    // The previous box's reduce-add has read the staging box.
-                    if (n > 0 && !(ok = mbar_wait(bar_st_free, (n - 1) & 1, kSiteBwdDQFree, abort_flag))) break;
-                    // scale * dQ -> staging box (128 rows x 32 fp32, 128-byte
-                    // swizzle: conflict-free 16-byte stores).
-                    const uint32_t box = sDQ + row * 128;
+                    const uint32_t box = sDQ + c * Cfg::kBox + row * 128;
 #pragma unroll
                     for (int v = 0; v < 8; ++v)
                         st_shared_v4(box + ((v ^ (row & 7)) << 4),
@@ -459,58 +449,44 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                                      __float_as_uint(__uint_as_float(r[c * 32 + 4 * v + 1]) * p.scale),
                                      __float_as_uint(__uint_as_float(r[c * 32 + 4 * v + 2]) * p.scale),
                                      __float_as_uint(__uint_as_float(r[c * 32 + 4 * v + 3]) * p.scale));
-                    fence_proxy_async_smem();
-                    mbar_arrive(bar_st_full);
                 }
+                fence_proxy_async_smem();
+                mbar_arrive(bar_st_full);
             }
         }
     } else {
         // ---------------------------------------------- compute warpgroups
-        // Thread = (key row, half): warps w and w+4 share TMEM lane quarter
-        // w % 4; warpgroup g takes queries [64g, 64g + 64) of S^T/dP^T and half
-        // of the dK/dV columns in the epilogue.
+        // Thread = (row, half): warps w and w+4 share TMEM lane quarter w % 4;
+        // warpgroup g takes columns [64g, 64g + 64) of S/dP and half of dK/dV.
         const int g = warp >> 2;
         const int row = (warp & 3) * 32 + lane;
         const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t tS = tmem + lane_off + Cfg::kColS + 64 * g, tDP = tmem + lane_off + Cfg::kColDP + 64 * g;
-        const int key = j * 128 + row;
-        const bool kvalid = key < p.Nkv;
-        // Stage the LSE (log2 domain) and Delta of query tile `it`: thread
-        // (g, row) loads entry `row` of array g.
-        auto load_stats = [&](int it) {
+        // Row statistics of the next query tile, loaded one step ahead.
+        auto row_stats = [&](int it, float &lse2, float &dlt) {
             const int q = (i0 + it) * 128 + row;
-            float v = g ? 0.f : INFINITY;  // +inf LSE: the query contributes nothing
-            if (q < p.Nq) {
-                if (g == 0) {
-                    const float l = __ldg(p.lse + (int64_t)bh * p.Nq + q);
-                    if (l != -INFINITY) v = l * 1.4426950408889634f;
-                } else {
-                    v = __ldg(p.delta + (int64_t)bh * p.Nq + q);
-                }
+            lse2 = INFINITY;  // +inf: the row contributes nothing
+            dlt = 0.f;
+            if (it < n_it && q < p.Nq) {
+                const float l = __ldg(p.lse + (int64_t)bh * p.Nq + q);
+                if (l != -INFINITY) lse2 = l * 1.4426950408889634f;
+                dlt = __ldg(p.delta + (int64_t)bh * p.Nq + q);
             }
-            stats[(it & 1) * 256 + g * 128 + row] = v;
-            mbar_arrive(bar_stats(it & 1));
         };
-        const uint32_t sStats = smem_u32(stats);
-        auto stat4 = [&](int buf, int arr, int c) {  // stats[buf][arr][64g + 4c .. +3]
-            float4 v;
-            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-                         : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                         : "r"(sStats + 4u * (buf * 256 + arr * 128 + 64 * g + 4 * c)));
-            return v;
-        };
-        load_stats(0);
+        float lse2_n, dlt_n;
+        row_stats(0, lse2_n, dlt_n);
         bool ok = n_it > 0;
         for (int it = 0; it < n_it && ok; ++it) {
             const uint32_t ph = it & 1;
-            const int buf = it & 1;
-            // Queries of this half visible to the key: columns [lo, 64).
-            int lo = kvalid ? 0 : 64;
-            if (p.causal && kvalid) lo = min(64, max(0, key - ((i0 + it) * 128 + 64 * g)));
+            const int q = (i0 + it) * 128 + row;
+            const float lse2 = lse2_n, dlt = dlt_n;
+            row_stats(it + 1, lse2_n, dlt_n);
+            // Keys of this tile (and this half) the row may see: [0, lim).
+            int lim = min(128, p.Nkv - j * 128);
+            if (p.causal) lim = min(lim, max(0, q - j * 128 + 1));
+            lim -= 64 * g;
 
-            if (!(ok = mbar_wait(bar_s, ph, kSiteBwdS, abort_flag) &&
-                       mbar_wait(bar_stats(buf), (it >> 1) & 1, kSiteBwdS, abort_flag)))
-                break;
+            if (!(ok = mbar_wait(bar_s, ph, kSiteBwdS, abort_flag))) break;
             if (row == 0 && g == 0) GAE_TRACE(kBtS, it);
             tc_fence_after();
             uint32_t pk[32];
@@ -519,37 +495,33 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                 tmem_ld32(tS, r0);
                 tmem_ld32(tS + 32, r1);
                 tmem_wait_ld();
-                const uint64_t sl2x2 = f2_pack(p.scale_log2, p.scale_log2);
+                const uint64_t sl2x2 = f2_pack(p.scale_log2, p.scale_log2), nl2 = f2_pack(-lse2, -lse2);
 #pragma unroll
-                for (int c4 = 0; c4 < 16; ++c4) {
-                    const float4 l4 = stat4(buf, 0, c4);
-                    const uint32_t *r = (c4 < 8) ? r0 : r1;
-                    const int rb = (c4 & 7) * 4;
-#pragma unroll
-                    for (int hp = 0; hp < 2; ++hp) {
-                        const int e = 2 * c4 + hp, col = 2 * e;
-                        const float la = hp ? l4.z : l4.x, lb = hp ? l4.w : l4.y;
-                        const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[rb + 2 * hp]), __uint_as_float(r[rb + 2 * hp + 1])),
-                                                  sl2x2, f2_pack(-la, -lb));
-                        float p0, p1;
-                        if (kBwdPolyPeriod > 0 && e % kBwdPolyPeriod == kBwdPolyPeriod - 1) {
-                            exp2_poly_x2(x, p0, p1);  // this pair on the FMA pipe
-                        } else {
-                            float x0, x1;
-                            f2_unpack(x, x0, x1);
-                            p0 = ex2_approx(x0);
-                            p1 = ex2_approx(x1);
-                        }
-                        p0 = (col >= lo) ? p0 : 0.f;
-                        p1 = (col + 1 >= lo) ? p1 : 0.f;
-                        pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
+                for (int e = 0; e < 32; ++e) {
+                    const uint32_t *r = (e < 16) ? r0 : r1;
+                    const int ee = e & 15, k0 = 2 * e;
+                    const uint64_t x = f2_fma(f2_pack(__uint_as_float(r[2 * ee]), __uint_as_float(r[2 * ee + 1])),
+                                              sl2x2, nl2);
+                    float p0, p1;
+                    if (kBwdPolyPeriod > 0 && e % kBwdPolyPeriod == kBwdPolyPeriod - 1) {
+                        exp2_poly_x2(x, p0, p1);  // this pair on the FMA pipe
+                    } else {
+                        float x0, x1;
+                        f2_unpack(x, x0, x1);
+                        p0 = ex2_approx(x0);
+                        p1 = ex2_approx(x1);
                     }
+                    p0 = (k0 < lim) ? p0 : 0.f;
+                    p1 = (k0 + 1 < lim) ? p1 : 0.f;
+                    pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }
             }
-            // P^T over the first 32 of this half's columns (its own S^T values).
-            tmem_st16(tS, pk);
-            tmem_st16(tS + 16, pk + 16);
-            tmem_wait_st();
+            // dS_{i-1} stays in the tile until dQ_{i-1}, its last reader, completed.
+            if (it > 0 && !(ok = mbar_wait(bar_dq, (it - 1) & 1, kSiteBwdDQ, abort_flag))) break;
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+                st_shared_v4(sPS + sw128_chunk(row, 8 * g + c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(bar_p);
             if (row == 0 && g == 0) GAE_TRACE(kBtPDone, it);
@@ -563,37 +535,30 @@ __global__ void __launch_bounds__(480, 1) attn_bwd_sm100_kernel(const __grid_con
                 tmem_ld32(tDP + 32, r1);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c4 = 0; c4 < 16; ++c4) {
-                    const float4 d4 = stat4(buf, 1, c4);
-                    const uint32_t *r = (c4 < 8) ? r0 : r1;
-                    const int rb = (c4 & 7) * 4;
-#pragma unroll
-                    for (int hp = 0; hp < 2; ++hp) {
-                        const int e = 2 * c4 + hp;
-                        const float da = hp ? d4.z : d4.x, db = hp ? d4.w : d4.y;
-                        float p0, p1;
-                        unpack2<kBF16>(pk[e], p0, p1);
-                        const float d0 = p0 * (__uint_as_float(r[rb + 2 * hp]) - da);
-                        const float d1 = p1 * (__uint_as_float(r[rb + 2 * hp + 1]) - db);
-                        pk[e] = kBF16 ? pack_bf16x2(d0, d1) : pack_f16x2(d0, d1);  // now dS^T
-                    }
+                for (int e = 0; e < 16; ++e) {
+                    float p0, p1;
+                    unpack2<kBF16>(pk[e], p0, p1);
+                    pk[e] = kBF16 ? pack_bf16x2(p0 * (__uint_as_float(r0[2 * e]) - dlt),
+                                                p1 * (__uint_as_float(r0[2 * e + 1]) - dlt))
+                                  : pack_f16x2(p0 * (__uint_as_float(r0[2 * e]) - dlt),
+                                               p1 * (__uint_as_float(r0[2 * e + 1]) - dlt));
+                    unpack2<kBF16>(pk[16 + e], p0, p1);
+                    pk[16 + e] = kBF16 ? pack_bf16x2(p0 * (__uint_as_float(r1[2 * e]) - dlt),
+                                                     p1 * (__uint_as_float(r1[2 * e + 1]) - dlt))
+                                       : pack_f16x2(p0 * (__uint_as_float(r1[2 * e]) - dlt),
+                                                    p1 * (__uint_as_float(r1[2 * e + 1]) - dlt));
                 }
             }
-            tmem_st16(tDP, pk);
-            tmem_st16(tDP + 16, pk + 16);
-            // dS rows (keys) for the dQ GEMM; the previous step's dQ, the tile's
-            // last reader, completed before dP^T_i could be issued.
+            tc_fence_before();
+            // P_i stays in the tile until the dV_i MMA that reads it has completed.
+            if (!(ok = mbar_wait(bar_pc, ph, kSiteBwdP, abort_flag))) break;
+            if (row == 0 && g == 0) GAE_TRACE(kBtPC, it);
 #pragma unroll
             for (int c = 0; c < 8; ++c)
                 st_shared_v4(sPS + sw128_chunk(row, 8 * g + c), pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
             fence_proxy_async_smem();
-            tmem_wait_st();
-            tc_fence_before();
             mbar_arrive(bar_ds);
             if (row == 0 && g == 0) GAE_TRACE(kBtDSDone, it);
-            // The other buffer was last read in step it-1, which every thread
-            // finished before dP^T_i could be issued.
-            if (it + 1 < n_it) load_stats(it + 1);
         }
         // Epilogue: this half of dV and scale * dK of the key tile -> global.
         if (ok && mbar_wait(bar_done, 0, kSiteBwdDone, abort_flag)) {
