@@ -39,6 +39,22 @@ REF_SYMPHONY_PATH = os.path.join(_HERE, "_ref", "libref_symphony.so")
 REF_SYMPHONY128_PATH = os.path.join(_HERE, "_ref", "libref_symphony128.so")
 
 
+REF_WALLER_PATH = os.path.join(_HERE, "_ref", "libref_waller.so")
+
+
+def ref_waller():
+    """ctypes handle on the reference's own fp32 Waller operator kernels
+    (cuda_src/waller_operator.cu, built by oracle/ref_waller_operator.cu), or
+    None where they were not built.  Device pointers."""
+    if not os.path.exists(REF_WALLER_PATH):
+        return None
+    L = C.CDLL(REF_WALLER_PATH)
+    vp = C.c_void_p
+    L.ref_waller_operator_fwd.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_float, vp]
+    L.ref_waller_operator_multihead_fwd.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_float, vp]
+    return L
+
+
 def ref_symphony128():
     """ctypes handle on the reference's head_dim-128 fused layer kernel
     (waller_fused_realistic.cu, built by oracle/ref_symphony_realistic.cu),

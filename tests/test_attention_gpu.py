@@ -238,3 +238,42 @@ def test_ate_gpu_backend_api(gae, ora):
     out = gae.AteGpu.new().waller_operator(q, k, v, n, d, 1 / math.sqrt(d)).reshape(n, d)
     ref = ora.waller_operator(q, k, v, n, d, 1 / math.sqrt(d), causal=True).reshape(n, d)
     assert rel_scale(out, ref) <= 1e-5
+
+
+def test_reference_waller_kernels_pin_oracle_and_product(gae, ora):
+    """The reference's own fp32 Waller kernels (cuda_src/waller_operator.cu:
+    12-100, built from its source into oracle/_ref) against the oracle's
+    restatement and this library's fp32 and bf16 paths on the same inputs
+    (fp32: max-abs <= 1e-5 of the largest output; bf16: 2e-2 max-abs)."""
+    L = ora.ref_waller()
+    if L is None:
+        pytest.skip("reference Waller kernels not built (no reference tree where build() ran)")
+    rng = np.random.default_rng(23)
+    st = torch.cuda.current_stream().cuda_stream
+    # single head [N, d], the reference's own layout
+    n, d = 1000, 64
+    q, k, v = (rng.standard_normal(n * d).astype(np.float32) for _ in range(3))
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    od = torch.empty_like(qd)
+    assert L.ref_waller_operator_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(), n, d,
+                                     0.125, st) == 0
+    torch.cuda.synchronize()
+    ref_gpu = od.cpu().numpy().reshape(n, d)
+    assert rel_scale(ora.waller_operator(q, k, v, n, d, 0.125, causal=True).reshape(n, d), ref_gpu) <= 1e-5
+    assert rel_scale(gae.waller_operator(q, k, v, n, d, 0.125).reshape(n, d), ref_gpu) <= 1e-5
+    # multi-head [H, N, d]
+    h, n, d = 4, 777, 128
+    q, k, v = (rng.standard_normal((1, h, n, d)).astype(np.float32) for _ in range(3))
+    qd, kd, vd = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    od = torch.empty_like(qd)
+    scale = 1 / math.sqrt(d)
+    assert L.ref_waller_operator_multihead_fwd(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), od.data_ptr(),
+                                               n, d, h, scale, st) == 0
+    torch.cuda.synchronize()
+    ref_gpu = od.cpu().numpy()
+    o32 = gae.attention(qd, kd, vd, causal=True)
+    assert rel_scale(o32.cpu().numpy(), ref_gpu) <= 1e-5
+    o16 = gae.attention(qd.bfloat16(), kd.bfloat16(), vd.bfloat16(), causal=True)
+    ref16 = ora.attention_batched(*(t.bfloat16().float().cpu().numpy() for t in (qd, kd, vd)), scale, True)
+    assert float(np.abs(o16.float().cpu().numpy() - ref16).max()) <= BF16_TOL
+    assert float(np.abs(ref16 - ref_gpu).max()) <= 5e-2  # bf16 input rounding only
