@@ -55,6 +55,21 @@ def ref_waller():
     return L
 
 
+REF_WALLER_INT8_PATH = os.path.join(_HERE, "_ref", "libref_waller_int8.so")
+
+
+def ref_waller_int8():
+    """ctypes handle on the reference's own INT8 Waller kernel
+    (cuda_src/waller_operator_int8.cu, built by oracle/ref_waller_int8.cu), or
+    None where it was not built.  Device pointers."""
+    if not os.path.exists(REF_WALLER_INT8_PATH):
+        return None
+    L = C.CDLL(REF_WALLER_INT8_PATH)
+    vp = C.c_void_p
+    L.ref_waller_int8_fwd.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_float, C.c_float, vp]
+    return L
+
+
 def ref_symphony128():
     """ctypes handle on the reference's head_dim-128 fused layer kernel
     (waller_fused_realistic.cu, built by oracle/ref_symphony_realistic.cu),

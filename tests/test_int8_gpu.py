@@ -78,3 +78,33 @@ def test_int8_rejects_bad_shapes(gae):
     v = torch.zeros(1, 128, 64, dtype=torch.bfloat16, device="cuda")
     with pytest.raises(gae.GAEError):
         gae.attention_int8(q, q, s, s, v)
+
+
+def test_reference_int8_kernel_pins_oracle_and_product(gae, ora):
+    """The reference's own INT8 Waller kernel (cuda_src/waller_operator_int8.cu:
+    27-68, built from its source into oracle/_ref: causal, one global
+    qk_scale, V int8 / v_scale) against the oracle's INT8 restatement (unit row
+    scales, the same scale, V = v / v_scale in fp32: max-abs <= 1e-5 of the
+    largest output) and this library's INT8 attention (V rounded to bf16,
+    output bf16: 2e-2 max-abs)."""
+    L = ora.ref_waller_int8()
+    if L is None:
+        pytest.skip("reference INT8 kernel not built (no reference tree where build() ran)")
+    rng = np.random.default_rng(31)
+    n, d = 1000, 128
+    q, k, v = (rng.integers(-127, 128, (n, d)).astype(np.int8) for _ in range(3))
+    qk_scale, v_scale = 1.0 / (math.sqrt(d) * 127.0 * 8.0), 127.0
+    dev = [torch.from_numpy(a).cuda() for a in (q, k, v)]
+    od = torch.empty(n, d, dtype=torch.float32, device="cuda")
+    assert L.ref_waller_int8_fwd(dev[0].data_ptr(), dev[1].data_ptr(), dev[2].data_ptr(), od.data_ptr(), n, d,
+                                 qk_scale, v_scale, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    ref_gpu = od.cpu().numpy()
+    ones = np.ones((1, n), np.float32)
+    vf = (v.astype(np.float32) / np.float32(v_scale))
+    ora_out = ora.attention_int8(q[None], k[None], ones, ones, vf[None], qk_scale, causal=True)[0]
+    assert float(np.abs(ora_out - ref_gpu).max()) <= 1e-5 * float(np.abs(ref_gpu).max())
+    got = gae.attention_int8(dev[0][None].contiguous(), dev[1][None].contiguous(),
+                             torch.ones(1, n, device="cuda"), torch.ones(1, n, device="cuda"),
+                             torch.from_numpy(vf[None]).cuda().bfloat16(), causal=True, scale=qk_scale)
+    assert float(np.abs(got.float().cpu().numpy()[0] - ref_gpu).max()) <= 2e-2
