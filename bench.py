@@ -59,6 +59,9 @@ WORKLOADS = {
     "long": dict(B=1, H=8, N=131072, D=128, causal=True, cfg="config5-131072"),
     "mha64": dict(B=8, H=12, N=2048, D=64, causal=True, cfg="config4-attention-d64"),
     "ring": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M", ring=True),
+    # sequence-parallel backward of the same sequence (no reference counterpart)
+    "ring-bwd": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ring-1M-backward", ring=True,
+                     sp="ring-bwd", metric="ring attention backward TFLOPS (bf16 d=128)"),
     "ulysses": dict(B=1, H=8, N=1048576, D=128, causal=True, cfg="config5-ulysses-1M", ring=True,
                     sp="ulysses"),
     "int8": dict(B=1, H=32, N=16384, D=128, causal=False, cfg="config3-int8", int8=True),
@@ -228,7 +231,7 @@ def cpu_sample(w, slices=8, rows_cap=None):
         flops = 4.0 * D * n_rows * N * slices
         return (flops / dt / 1e12, dt, f"{slices} head(s) x {n_rows} query rows, full key range each",
                 oracle.num_threads())
-    if w.get("bwd"):
+    if w.get("bwd") or w.get("sp") == "ring-bwd":
         # gradients of one (batch, head) slice over its first `rows_cap` tokens
         # (a causal prefix is a complete problem of its own)
         n = N if rows_cap is None else min(N, rows_cap)
@@ -285,7 +288,7 @@ def run_reference(args, w):
             v, s, desc, threads = cpu_sample(w)
             vals.append(v); secs.append(s)
         return _print_reference(args, w, statistics.mean(vals), statistics.mean(secs), desc, threads)
-    if w.get("bwd"):
+    if w.get("bwd") or w.get("sp") == "ring-bwd":
         budget = 120.0 / (args.steps + args.warmup)
         _, s_cal, _, _ = cpu_sample(w, slices=1, rows_cap=512)
         n = int(min(w["N"], 512 * math.sqrt(budget / max(s_cal, 1e-6))))
@@ -511,7 +514,20 @@ def main():
         out = torch.empty_like(q)
         flops = attn_flops(B, H, N, N, D, causal) / world  # per rank share of the job
 
-        if w.get("sp") == "ulysses":
+        if w.get("sp") == "ring-bwd":
+            q0 = q
+            o0, lse0 = ring.ring_attention(q0, k, v, causal=causal, return_lse=True)
+            g = torch.Generator(device="cpu").manual_seed(2000 + rank)
+            do0 = torch.randn(q0.shape, generator=g).to(torch.bfloat16).to(dev)
+            q = (q0, o0, do0, lse0)
+            out = torch.empty((3,) + tuple(q0.shape), dtype=q0.dtype, device=dev)
+            flops = 2.5 * attn_flops(B, H, N, N, D, causal) / world
+
+            def run_step(q, k, v):
+                for dst, src in zip(out, ring.ring_attention_backward(q[0], k, v, q[1], q[2], q[3],
+                                                                      causal=causal)):
+                    dst.copy_(src)
+        elif w.get("sp") == "ulysses":
             from gae_b200 import ulysses
 
             def run_step(q, k, v):
@@ -579,6 +595,8 @@ def main():
         launches_per_step = 3  # prep, attention, post
     if is_bwd:
         launches_per_step = 3  # dO.O row sums, backward, dQ conversion (plus one memset)
+    if is_ring and w.get("sp") == "ring-bwd":
+        launches_per_step = 3 * (3 + 2 * (world - 1))  # block pairs (zig-zag) x 3 launches
 
     # ---- end to end through the public API with host buffers ---------------
     def flat(t):
@@ -594,7 +612,7 @@ def main():
             return ts[0], ts[0], ts[0]
         if is_int8:
             return (ts[0], ts[1]), (ts[2], ts[3]), ts[4]
-        if is_bwd:
+        if is_bwd or (is_ring and w.get("sp") == "ring-bwd"):
             return (ts[0], ts[1], ts[2], ts[3]), ts[4], ts[5]
         return ts[0], ts[1], ts[2]
 
@@ -665,7 +683,7 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         if is_sym:
             v_cpu, s_cpu, desc, threads = cpu_sample(w, rows_cap=16384)
-        elif is_bwd:
+        elif is_bwd or w.get("sp") == "ring-bwd":
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=1, rows_cap=1024)
         elif w.get("int8"):
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=2, rows_cap=2048)
