@@ -118,13 +118,23 @@ struct AttnCfg {
     // Q loads while the current one runs; at 128 shared memory allows one.
     static constexpr int kQStages = (D == 64) ? 2 : 1;
     static constexpr int kRingBytes = kStages * kSlotBytes;
-    static constexpr int kBarOffset = kQStages * kQBytes + kRingBytes;
+    // Row sums by the tensor core (16-bit modes at head_dim 64, where the
+    // softmax instruction stream is the bound and the tensor pipe has room):
+    // P.V runs with 16 more B columns of ones read from a constant panel, so
+    // O's column D accumulates sum(P) -- rescaled with O, from the same
+    // rounded P as the numerator -- instead of the softmax warps adding it up.
+    static constexpr bool kMmaRowSum = (D == 64) && !kInt8;
+    static constexpr int kOCols = D + (kMmaRowSum ? 16 : 0);
+    static constexpr int kOnesBytes = kMmaRowSum ? kBoxBytes : 0;
+    static constexpr int kOffOnes = kQStages * kQBytes + kRingBytes;
+    static constexpr int kBarOffset = kOffOnes + kOnesBytes;
     // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done, q_empty,
     // q_full / q_empty of the second Q stage
     static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 2;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
     static constexpr uint32_t kTmemCols = 512;
-    static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + D;
+    static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + kOCols;
+    static_assert(256 + 2 * kOCols <= 512, "TMEM budget");
     static constexpr int kThreads = 384;
     // The producer warps' unit loop needs more than 72 registers (96 with the
     // int8 scale loads); the softmax warps take the rest.
@@ -254,6 +264,14 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         *abort_flag = 0;
         fence_mbar_init();
     }
+    if constexpr (Cfg::kMmaRowSum) {
+        // The constant B panel of ones (whole panel, so the swizzle is moot).
+        const uint32_t one2 = kBF16 ? 0x3F803F80u : 0x3C003C00u;
+        uint4 *ones = reinterpret_cast<uint4 *>(smem + Cfg::kOffOnes);
+        for (int i = threadIdx.x; i < Cfg::kOnesBytes / 16; i += blockDim.x)
+            ones[i] = make_uint4(one2, one2, one2, one2);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
     if (warp == 9 && any_work) {
         tmem_alloc(smem_u32(tmem_base_slot), Cfg::kTmemCols);
         tmem_relinquish();
@@ -330,7 +348,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         if (lane == 0 && any_work) {
             constexpr uint32_t idesc_qk =
                 Cfg::kInt8 ? idesc_i8(128, 128) : idesc_f16(128, 128, kBF16, false, false);
-            constexpr uint32_t idesc_pv = idesc_f16(128, D, kBF16, false, true);
+            constexpr uint32_t idesc_pv = idesc_f16(128, Cfg::kOCols, kBF16, false, true);
             auto issue_qk = [&](int i, int slot, uint32_t q_base) {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
                 const uint32_t qa = q_base + i * Cfg::kQTileBytes;
@@ -354,7 +372,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
 #pragma unroll
                 for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk) {
                     umma_f16_ts(d_tmem, p_tmem + kk * 8,
-                                smem_desc_sw128(vb + kk * 16 * 128, Cfg::kBoxBytes, 1024), idesc_pv,
+                                smem_desc_sw128(vb + kk * 16 * 128,
+                                                Cfg::kMmaRowSum ? (base + Cfg::kOffOnes) - vb : Cfg::kBoxBytes, 1024),
+                                idesc_pv,
                                 (acc || kk > 0) ? 1u : 0u);
                 }
             };
@@ -586,14 +606,13 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 }
                 tmem_st16(tS + c * 16, pk);
             }
-            float rs;
-            {
-                float a0, a1, b0, b1;
+            if constexpr (!Cfg::kMmaRowSum) {
+                float a0, a1;
                 f2_unpack(f2_add(f2_add(acc2[0], acc2[1]), f2_add(acc2[2], acc2[3])), a0, a1);
-                (void)b0; (void)b1;
-                rs = a0 + a1;
+                l_run = l_run * alpha + (a0 + a1);
+            } else {
+                (void)acc2;
             }
-            l_run = l_run * alpha + rs;
             // Rescale O_i when the base moved (warp-uniform: tcgen05.ld/st are
             // warp-collective).  PV_i(j-1) has completed: its commit preceded S_i(j)'s.
             if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -606,6 +625,14 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
                     tmem_st32(tO + c * 32, r);
                 }
+                if constexpr (Cfg::kMmaRowSum) {  // the row-sum columns
+                    uint32_t r[16];
+                    tmem_ld16(tO + D, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                    tmem_st16(tO + D, r);
+                }
             }
             tmem_wait_st();
             tc_fence_before();
@@ -616,9 +643,19 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
 
         // Epilogue: O_i / l -> global; log-sum-exp.
         const bool row_valid = q_local < p.Nq;
-        const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
         if (row == 0 && grp == 0) GAE_TRACE(kTrEpiStart, au);
         if (n_kv > 0 && ok) ok = mbar_wait(bar_o(grp), au & 1, kSiteO, abort_flag);
+        if constexpr (Cfg::kMmaRowSum) {
+            l_run = 0.f;
+            if (n_kv > 0 && ok) {
+                tc_fence_after();
+                uint32_t r[16];
+                tmem_ld16(tO + D, r);
+                tmem_wait_ld();
+                l_run = __uint_as_float(r[0]);
+            }
+        }
+        const float inv_l = (l_run > 0.f) ? 1.f / l_run : 0.f;
         if (n_kv > 0 && ok) {
             tc_fence_after();
             char *orow = reinterpret_cast<char *>(p.o) +
