@@ -4,13 +4,14 @@
                     [--workload mha|mha-noncausal|long]
 
 Workloads (synthetic inputs, numpy/torch seeded, iid N(0,1) -> bf16):
-  mha            BASELINE config 2, causal: B=4, H=16, N=8192, head_dim=128 (default)
+  mha            BASELINE config 2, causal: B=4, H=16, N=8192, head_dim=128
   mha-noncausal  the same, non-causal
   long           config 5, causal: one sequence, H=8, head_dim=128, N=131072
   mha64          the attention of config 4 alone: B=8, H=12, N=2048, head_dim=64, causal
   ring           config 5, causal: one sequence of N=1,048,576 (H=8, head_dim=128)
                  sharded over the N GPUs (contiguous N/P shards, ring attention with
-                 zig-zag balance, K/V rotated by NCCL send/recv; strong scaling)
+                 zig-zag balance, K/V rotated by NCCL send/recv; strong scaling).
+                 The default: `--gpus N` measures the north-star ring curve.
   ulysses        config 5 like `ring`, but sequence parallel by head/sequence
                  all-to-all (each rank attends the whole sequence for H/P heads)
   int8           config 3: B=1, H=32, N=16384, head_dim=128, non-causal; Q, K
@@ -150,8 +151,12 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        # A sample stamps the end of its period: keep every sample whose
+        # period overlaps [t0, t1]; a region shorter than one period still
+        # gets the sample that covers it.
+        slack = self.period_ms / 1000.0
         for ts, ln in list(self.samples):
-            if self.t0 is not None and not (self.t0 <= ts <= self.t1):
+            if self.t0 is not None and not (self.t0 <= ts <= self.t1 + slack):
                 continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
@@ -201,6 +206,7 @@ def cpu_sample(w, slices=8, rows_cap=None):
     slice.  Returns (TFLOPS, seconds, description, threads)."""
     import numpy as np
     from oracle import oracle
+    oracle.use_all_cores()
     N, D = w["N"], w["D"]
     rng = np.random.default_rng(1234)
     if w.get("gpt2"):
@@ -396,7 +402,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="gae", choices=["gae", "reference"])
-    ap.add_argument("--workload", default="mha", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="ring", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--reference-kernel", action="store_true",
                     help="with --impl reference --workload symphony: time the reference's own "
@@ -688,7 +694,12 @@ def main():
         elif w.get("int8"):
             v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=2, rows_cap=2048)
         else:
-            v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=None if w["N"] <= 16384 else 2048)
+            if w["N"] <= 16384:
+                v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8)
+            elif w["N"] <= 131072:
+                v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=8, rows_cap=2048)
+            else:  # 1M tokens: one head, 512 rows over the sequence (~10 s on 32 cores)
+                v_cpu, s_cpu, desc, threads = cpu_sample(w, slices=1, rows_cap=512)
         cpu = {"value": v_cpu, "unit": "TFLOPS", "cores": threads, "kind": "port",
                "sample": desc + f" ({s_cpu:.1f} s)"}
 

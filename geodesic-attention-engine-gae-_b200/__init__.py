@@ -125,6 +125,13 @@ def lib():
     L.gae_symphony_workspace_bytes.restype = sz
     L.gae_symphony_workspace_bytes.argtypes = [i64, i64]
     L.gae_symphony_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp, vp, sz, vp]
+    L.gae_layernorm_f32_host.argtypes = [vp, vp, vp, sz, C.c_float, vp]
+    L.gae_layernorm_batched_f32_host.argtypes = [vp, vp, vp, sz, sz, C.c_float, vp]
+    L.gae_mlp_block_f32_host.argtypes = [vp, vp, vp, vp, vp, sz, sz, sz, vp]
+    L.gae_fused_mlp_layernorm_f32_host.argtypes = [vp] * 8 + [sz, sz, C.c_float, sz, vp]
+    L.gae_transformer_block_forward_f32_host.argtypes = [vp, vp, sz, vp]
+    L.gae_crate_linear_f32.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, C.c_int, vp]
+    L.gae_crate_layernorm_f32.argtypes = [vp, vp, vp, vp, i64, i64, C.c_float, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     L.gae_debug_wait_timeout.argtypes = [C.c_uint64, vp]
     _lib = L
@@ -695,78 +702,98 @@ def layer_stack_forward(layers, x, out=None, workspace=None, stream=None):
     return out
 
 
-def _dev_f32(a, shape=None, dtype=None):
-    torch = _torch()
-    t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
-    if shape is not None:
-        t = t.reshape(shape)
-    t = t.to("cuda")
-    return t.to(dtype) if dtype is not None else t
+def _slice(x, n, what):
+    a = np.ascontiguousarray(np.asarray(x, dtype=np.float32).reshape(-1))
+    if a.size < n:
+        # The crate indexes these slices directly and panics on a short one.
+        raise GAEError(1, f"{what} has {a.size} elements, need {n}")
+    return a
+
+
+def _ptr(a):
+    return a.ctypes.data
 
 
 def layernorm_batched(input, gamma, beta, batch_size: int, hidden_dim: int, eps: float):
-    """ate::layernorm_batched (rust_src/src/layernorm.rs:20-47) on the GPU
-    LayerNorm kernel: host f32 slices in, host f32 out; rows staged in bf16
-    (hidden_dim % 8 == 0, <= 4096)."""
-    torch = _torch()
+    """ate::layernorm_batched (rust_src/src/layernorm.rs:20-47) through
+    gae_layernorm_batched_f32_host: fp32, the crate's Welford statistics in
+    its order (bit-identical results).  Host f32 in, host f32 out."""
     n = batch_size * hidden_dim
-    x = _dev_f32(_host_f32(input, n)[:n], (batch_size, hidden_dim), torch.bfloat16)
-    y = layernorm_rows(x, _dev_f32(_host_f32(gamma, hidden_dim)[:hidden_dim]),
-                       _dev_f32(_host_f32(beta, hidden_dim)[:hidden_dim]), eps)
-    return y.float().cpu().numpy().reshape(-1)
+    x = _slice(input, n, "input")
+    g, b = _slice(gamma, hidden_dim, "gamma"), _slice(beta, hidden_dim, "beta")
+    out = np.empty(n, np.float32)
+    _check(lib().gae_layernorm_batched_f32_host(_ptr(x), _ptr(g), _ptr(b), batch_size, hidden_dim,
+                                                eps, _ptr(out)))
+    return out
 
 
 def layernorm(input, gamma, beta, eps: float):
-    """ate::layernorm (layernorm.rs:6-17): one row."""
-    d = len(gamma)
-    return layernorm_batched(input, gamma, beta, 1, d, eps)
-
-
-def _mlp_device(x, w1, b1, w2, b2, hidden, mlp, res=None):
-    torch = _torch()
-    # The crate stores W1 [hidden, mlp] and W2 [mlp, hidden] (input-major);
-    # the tensor-core GEMM takes W[out, in].
-    w1d = _dev_f32(np.asarray(w1, np.float32).reshape(hidden, mlp).T, None, torch.bfloat16).contiguous()
-    w2d = _dev_f32(np.asarray(w2, np.float32).reshape(mlp, hidden).T, None, torch.bfloat16).contiguous()
-    hid = linear(x, w1d, bias=_dev_f32(b1), gelu=True)
-    return linear(hid, w2d, bias=_dev_f32(b2), res=res)
+    """ate::layernorm (layernorm.rs:6-17): one row, the length of `input`."""
+    x = np.ascontiguousarray(np.asarray(input, dtype=np.float32).reshape(-1))
+    n = x.size
+    g, b = _slice(gamma, n, "gamma"), _slice(beta, n, "beta")
+    out = np.empty(n, np.float32)
+    _check(lib().gae_layernorm_f32_host(_ptr(x), _ptr(g), _ptr(b), n, eps, _ptr(out)))
+    return out
 
 
 def mlp_block(input, w1, b1, w2, b2, hidden_dim: int, mlp_dim: int):
     """ate::mlp_block (rust_src/src/mlp.rs:7-36): gelu(x @ W1 + b1) @ W2 + b2
-    on the tcgen05 GEMM with fused bias / tanh-GELU epilogues.  `input` may
-    hold several tokens (len = tokens * hidden_dim; the crate takes one);
-    hidden_dim and mlp_dim multiples of 256, bf16 activations."""
-    torch = _torch()
-    x = np.asarray(input, np.float32).reshape(-1, hidden_dim)
-    y = _mlp_device(_dev_f32(x, None, torch.bfloat16), w1, b1, w2, b2, hidden_dim, mlp_dim)
-    return y.float().cpu().numpy().reshape(-1)
+    in fp32 with the crate's sequential sums (gae_mlp_block_f32_host).
+    `input` may hold several tokens (len = tokens * hidden_dim; the crate
+    takes one); any widths."""
+    x = np.ascontiguousarray(np.asarray(input, dtype=np.float32).reshape(-1))
+    tokens = max(1, x.size // hidden_dim)
+    x = _slice(x, tokens * hidden_dim, "input")
+    a1, c1 = _slice(w1, hidden_dim * mlp_dim, "w1"), _slice(b1, mlp_dim, "b1")
+    a2, c2 = _slice(w2, hidden_dim * mlp_dim, "w2"), _slice(b2, hidden_dim, "b2")
+    out = np.empty(tokens * hidden_dim, np.float32)
+    _check(lib().gae_mlp_block_f32_host(_ptr(x), _ptr(a1), _ptr(c1), _ptr(a2), _ptr(c2), hidden_dim,
+                                        mlp_dim, tokens, _ptr(out)))
+    return out
 
 
 def fused_mlp_layernorm(input, residual, w1, b1, w2, b2, gamma, beta, hidden_dim: int,
                         mlp_dim: int, eps: float):
     """ate::fused_mlp_layernorm (mlp.rs:39-73): LayerNorm(mlp_block(x) +
-    residual); the residual add is fused into the second GEMM's epilogue."""
-    torch = _torch()
-    x = _dev_f32(np.asarray(input, np.float32).reshape(-1, hidden_dim), None, torch.bfloat16)
-    r = _dev_f32(np.asarray(residual, np.float32).reshape(-1, hidden_dim), None, torch.bfloat16)
-    y = _mlp_device(x, w1, b1, w2, b2, hidden_dim, mlp_dim, res=r)
-    out = layernorm_rows(y, _dev_f32(gamma), _dev_f32(beta), eps)
-    return out.float().cpu().numpy().reshape(-1)
+    residual) in fp32 (gae_fused_mlp_layernorm_f32_host), per token."""
+    x = np.ascontiguousarray(np.asarray(input, dtype=np.float32).reshape(-1))
+    tokens = max(1, x.size // hidden_dim)
+    n = tokens * hidden_dim
+    x, r = _slice(x, n, "input"), _slice(residual, n, "residual")
+    a1, c1 = _slice(w1, hidden_dim * mlp_dim, "w1"), _slice(b1, mlp_dim, "b1")
+    a2, c2 = _slice(w2, hidden_dim * mlp_dim, "w2"), _slice(b2, hidden_dim, "b2")
+    g, bt = _slice(gamma, hidden_dim, "gamma"), _slice(beta, hidden_dim, "beta")
+    out = np.empty(n, np.float32)
+    _check(lib().gae_fused_mlp_layernorm_f32_host(_ptr(x), _ptr(r), _ptr(a1), _ptr(c1), _ptr(a2),
+                                                  _ptr(c2), _ptr(g), _ptr(bt), hidden_dim, mlp_dim,
+                                                  eps, tokens, _ptr(out)))
+    return out
+
+
+class TransformerBlockF32(C.Structure):
+    """Mirror of gae_transformer_block_f32 (host pointers + config)."""
+    _fields_ = ([(n, C.c_void_p) for n in ("wq", "wk", "wv", "wo", "ln1_gamma", "ln1_beta", "w1",
+                                            "b1", "w2", "b2", "ln2_gamma", "ln2_beta")] +
+                [("hidden_dim", C.c_size_t), ("num_heads", C.c_size_t), ("head_dim", C.c_size_t),
+                 ("mlp_dim", C.c_size_t), ("eps", C.c_float)])
 
 
 class TransformerBlock:
-    """ate::TransformerBlock (rust_src/src/transformer.rs:36-120) on the GPU
-    kernels.  Weights keep the crate's layouts (wq/wk/wv/wo [h, h] as
-    W[out, in]; w1 [h, m]; w2 [m, h]); forward() reproduces the crate's demo
-    forward exactly as written (transformer.rs:87-120: per-token LN1 -> Wv ->
-    Wo + residual -> MLP + residual -> LN2, no cross-token attention) in bf16
-    on the tensor cores.  hidden_dim and mlp_dim must be multiples of 256."""
+    """ate::TransformerBlock (rust_src/src/transformer.rs:36-120) on the GPU.
+    Weights keep the crate's layouts (wq/wk/wv/wo [h, h] as W[out, in]; w1
+    [h, m]; w2 [m, h]); forward() reproduces the crate's demo forward exactly
+    as written (transformer.rs:87-120: per-token LN1 -> Wv -> Wo + residual ->
+    MLP + residual -> LN2, no cross-token attention) in fp32 with the crate's
+    operation order, through gae_transformer_block_forward_f32_host."""
+
+    _names = ("wq", "wk", "wv", "wo", "ln1_gamma", "ln1_beta", "w1", "b1", "w2", "b2",
+              "ln2_gamma", "ln2_beta")
 
     def __init__(self, config: TransformerConfig, **w):
         self.config = config
         for k, v in w.items():
-            setattr(self, k, np.asarray(v, np.float32))
+            setattr(self, k, np.ascontiguousarray(np.asarray(v, np.float32).reshape(-1)))
 
     @classmethod
     def new_random(cls, config: TransformerConfig):
@@ -778,20 +805,17 @@ class TransformerBlock:
                    b1=f(m, 0), w2=f(m * h, .02), b2=f(h, 0), ln2_gamma=f(h, 1), ln2_beta=f(h, 0))
 
     def forward(self, input, seq_len: int):
-        torch = _torch()
         cfg = self.config
         h, m = cfg.hidden_dim, cfg.mlp_dim
-        dev = "cuda"
-        bf = lambda a, shape: torch.from_numpy(np.ascontiguousarray(a, np.float32).reshape(shape)).to(dev).to(torch.bfloat16)
-        fp = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
-        x = bf(_host_f32(input, seq_len * h)[: seq_len * h], (seq_len, h))
-        n = layernorm_rows(x, fp(self.ln1_gamma), fp(self.ln1_beta), cfg.eps)
-        v = linear(n, bf(self.wv, (h, h)))
-        r1 = linear(v, bf(self.wo, (h, h)), res=x)
-        hid = linear(r1, bf(self.w1.reshape(h, m).T, (m, h)), bias=fp(self.b1), gelu=True)
-        mo = linear(hid, bf(self.w2.reshape(m, h).T, (h, m)), bias=fp(self.b2), res=r1)
-        out = layernorm_rows(mo, fp(self.ln2_gamma), fp(self.ln2_beta), cfg.eps)
-        return out.float().cpu().numpy().reshape(-1)
+        sizes = dict(wq=h * h, wk=h * h, wv=h * h, wo=h * h, ln1_gamma=h, ln1_beta=h, w1=h * m, b1=m,
+                     w2=m * h, b2=h, ln2_gamma=h, ln2_beta=h)
+        arrs = {n: _slice(getattr(self, n), sizes[n], n) for n in self._names}
+        blk = TransformerBlockF32(*(_ptr(arrs[n]) for n in self._names), h, cfg.num_heads,
+                                  cfg.head_dim, m, cfg.eps)
+        x = _slice(input, seq_len * h, "input")
+        out = np.empty(seq_len * h, np.float32)
+        _check(lib().gae_transformer_block_forward_f32_host(C.byref(blk), _ptr(x), seq_len, _ptr(out)))
+        return out
 
 
 class TuningFork(C.Structure):

@@ -21,6 +21,7 @@
 #include "attn_int8_sm100.cuh"
 #include "layer_sm100.cuh"
 #include "symphony.cuh"
+#include "crate_f32.cuh"
 
 namespace {
 
@@ -608,20 +609,31 @@ gae_status launch_layernorm(const void *x, const void *res, void *sum_out, void 
 // Workspace carve-up of one layer (bytes, each region 256-byte aligned):
 // ln [T, D], qkv [T, 3D], attn [T, D], x1 [T, D], hidden [T, F], and for the
 // stack one spare activation [T, D].
+// ok is false when a size would overflow (absurd shapes); callers reject those.
 struct LayerWs {
     size_t ln, qkv, attn, x1, hid, spare, total;
+    bool ok;
 };
 LayerWs layer_ws(int64_t T, int64_t D, int64_t F) {
-    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     LayerWs w;
+    memset(&w, 0, sizeof(w));
+    const int64_t lim = (int64_t)1 << 31;
+    if (T < 0 || D < 0 || F < 0 || T > lim || D > lim || F > lim) return w;
+    size_t td = 0, tf = 0;
+    if (__builtin_mul_overflow((size_t)T, (size_t)D * 6, &td) ||
+        __builtin_mul_overflow((size_t)T, (size_t)F * 2, &tf))
+        return w;
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t act = al((size_t)T * (size_t)D * 2);  // fits: T*D*6 did
     size_t o = 0;
-    w.ln = o; o += al(T * D * 2);
-    w.qkv = o; o += al(T * 3 * D * 2);
-    w.attn = o; o += al(T * D * 2);
-    w.x1 = o; o += al(T * D * 2);
-    w.hid = o; o += al(T * F * 2);
-    w.spare = o; o += al(T * D * 2);
+    w.ln = o; o += act;
+    w.qkv = o; o += al(td);
+    w.attn = o; o += act;
+    w.x1 = o; o += act;
+    w.hid = o; o += al(tf);
+    w.spare = o; o += act;
     w.total = o;
+    w.ok = o >= td && o >= tf;  // the sum of a few in-range terms cannot wrap below them
     return w;
 }
 
@@ -671,7 +683,10 @@ gae_status check_layer(const gae_layer_args *a, const gae_layer_weights *w) {
     const int64_t hd = a->d_model / a->heads;
     if (hd != 64 && hd != 128) return fail(GAE_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
     if (!a->x || !a->out || !a->workspace) return fail(GAE_ERR_INVALID_ARG, "NULL activation or workspace");
+    if (a->batch > ((int64_t)1 << 31) / a->seq)
+        return fail(GAE_ERR_INVALID_ARG, "batch*seq beyond 2^31 tokens");
     const LayerWs L = layer_ws(a->batch * a->seq, a->d_model, a->d_ff);
+    if (!L.ok) return fail(GAE_ERR_INVALID_ARG, "layer shape too large (workspace size overflows)");
     if (a->workspace_bytes < L.total)
         return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", a->workspace_bytes, L.total);
     const void *ps[12] = {w->ln1_gamma, w->ln1_beta, w->w_qkv, w->b_qkv, w->w_proj, w->b_proj,
@@ -693,6 +708,80 @@ gae_status launch_symphony_post(const float *x, const __half *attn, const float 
     return GAE_OK;
 }
 
+
+// ------------------------------------------------- crate fp32 layer functions
+// Device scratch of one host-memory call: every buffer is freed on scope exit.
+struct HostCall {
+    cudaStream_t st = nullptr;
+    void *bufs[16] = {};
+    int n = 0;
+    ~HostCall() {
+        if (st) cudaStreamSynchronize(st);
+        for (int i = 0; i < n; ++i) cudaFree(bufs[i]);
+        if (st) cudaStreamDestroy(st);
+    }
+    gae_status init() {
+        GAE_CUDA_TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+        return GAE_OK;
+    }
+    // Device copy of `count` host floats (src may be NULL: uninitialised).
+    gae_status dev(float **out, const float *src, size_t count) {
+        if (n >= 16) return fail(GAE_ERR_INVALID_ARG, "too many buffers");
+        void *p = nullptr;
+        GAE_CUDA_TRY(cudaMalloc(&p, (count ? count : 1) * sizeof(float)));
+        bufs[n++] = p;
+        if (src && count) GAE_CUDA_TRY(cudaMemcpyAsync(p, src, count * sizeof(float), cudaMemcpyHostToDevice, st));
+        *out = static_cast<float *>(p);
+        return GAE_OK;
+    }
+    gae_status back(float *dst, const float *src, size_t count) {
+        GAE_CUDA_TRY(cudaMemcpyAsync(dst, src, count * sizeof(float), cudaMemcpyDeviceToHost, st));
+        GAE_CUDA_TRY(cudaStreamSynchronize(st));
+        return GAE_OK;
+    }
+};
+
+gae_status launch_crate_linear(const float *x, const float *w, const float *bias, const float *res, float *y,
+                               int64_t M, int64_t N, int64_t K, int w_in_major, int epi, cudaStream_t st) {
+    if (M == 0 || N == 0) return GAE_OK;
+    if (!x || !w || !y || M < 0 || N < 0 || K < 0) return fail(GAE_ERR_INVALID_ARG, "invalid linear arguments");
+    if (epi == 2 && !res) return fail(GAE_ERR_INVALID_ARG, "residual epilogue without res");
+    if (epi < 0 || epi > 2) return fail(GAE_ERR_INVALID_ARG, "unknown epilogue %d", epi);
+    const int64_t gy = (M + gae::kCrateBM - 1) / gae::kCrateBM;
+    if (gy > 65535) return fail(GAE_ERR_UNSUPPORTED, "more than %lld tokens", 65535LL * gae::kCrateBM);
+    dim3 grid((unsigned)((N + gae::kCrateBN - 1) / gae::kCrateBN), (unsigned)gy);
+    if (w_in_major)
+        gae::crate_linear_f32_kernel<true><<<grid, 256, 0, st>>>(x, w, bias, res, y, M, N, K, epi);
+    else
+        gae::crate_linear_f32_kernel<false><<<grid, 256, 0, st>>>(x, w, bias, res, y, M, N, K, epi);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+gae_status launch_crate_layernorm(const float *x, const float *g, const float *b, float *y, int64_t rows,
+                                  int64_t d, float eps, cudaStream_t st) {
+    if (rows == 0 || d == 0) return GAE_OK;
+    if (!x || !g || !b || !y || rows < 0 || d < 0) return fail(GAE_ERR_INVALID_ARG, "invalid layernorm arguments");
+    const int64_t blocks = (rows + 127) / 128;
+    if (blocks > INT32_MAX) return fail(GAE_ERR_UNSUPPORTED, "too many rows");
+    gae::crate_layernorm_f32_kernel<<<(unsigned)blocks, 128, 0, st>>>(x, g, b, y, rows, d, eps);
+    GAE_CUDA_TRY(cudaGetLastError());
+    return GAE_OK;
+}
+
+// LayerNorm(mlp_block(x) + residual) over `tokens` rows (mlp.rs:39-73); on
+// device buffers, hid [tokens, mlp] and tmp [tokens, hidden] scratch.
+gae_status crate_fused_mlp_ln(const float *x, const float *res, const float *w1, const float *b1,
+                              const float *w2, const float *b2, const float *g, const float *bt,
+                              int64_t T, int64_t h, int64_t m, float eps, float *hid, float *tmp,
+                              float *out, cudaStream_t st) {
+    gae_status s;
+    if ((s = launch_crate_linear(x, w1, b1, nullptr, hid, T, m, h, 1, 1, st)) != GAE_OK) return s;
+    if ((s = launch_crate_linear(hid, w2, b2, res, tmp, T, h, m, 1, 2, st)) != GAE_OK) return s;
+    return launch_crate_layernorm(tmp, g, bt, out, T, h, eps, st);
+}
+
+bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
 }  // namespace
 
 // ==================================================================== C ABI
@@ -817,7 +906,9 @@ gae_status gae_lse_merge(void *o_acc, float *lse_acc, const void *o_part, const 
 
 size_t gae_layer_workspace_bytes(int64_t batch, int64_t seq, int64_t d_model, int64_t d_ff) {
     if (batch < 1 || seq < 1 || d_model < 1 || d_ff < 1) return 0;
-    return layer_ws(batch * seq, d_model, d_ff).total;
+    if (batch > ((int64_t)1 << 31) / seq) return 0;
+    const LayerWs L = layer_ws(batch * seq, d_model, d_ff);
+    return L.ok ? L.total : 0;
 }
 
 gae_status gae_layer_fwd(const gae_layer_args *a, const gae_layer_weights *w, void *stream) {
@@ -956,6 +1047,118 @@ gae_status gae_quantize_rows_int8(const void *x, gae_dtype dtype, int64_t rows, 
     return GAE_OK;
 }
 
+
+// ------------------------------------------------- crate fp32 layer functions
+gae_status gae_crate_linear_f32(const float *x, const float *w, const float *bias, const float *res, float *y,
+                                int64_t M, int64_t N, int64_t K, int w_in_major, int epilogue, void *stream) {
+    return launch_crate_linear(x, w, bias, res, y, M, N, K, w_in_major, epilogue,
+                               static_cast<cudaStream_t>(stream));
+}
+
+gae_status gae_crate_layernorm_f32(const float *x, const float *gamma, const float *beta, float *y,
+                                   int64_t rows, int64_t d, float eps, void *stream) {
+    return launch_crate_layernorm(x, gamma, beta, y, rows, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+gae_status gae_layernorm_batched_f32_host(const float *input, const float *gamma, const float *beta,
+                                          size_t batch, size_t hidden, float eps, float *out) {
+    size_t n = 0;
+    if (!mul_ok(batch, hidden, &n)) return fail(GAE_ERR_INVALID_ARG, "batch*hidden overflows");
+    if (n == 0) return GAE_OK;
+    if (!input || !gamma || !beta || !out) return fail(GAE_ERR_INVALID_ARG, "NULL host pointer");
+    HostCall c;
+    float *dx, *dg, *db, *dy;
+    gae_status s;
+    if ((s = c.init()) || (s = c.dev(&dx, input, n)) || (s = c.dev(&dg, gamma, hidden)) ||
+        (s = c.dev(&db, beta, hidden)) || (s = c.dev(&dy, nullptr, n)))
+        return s;
+    if ((s = launch_crate_layernorm(dx, dg, db, dy, (int64_t)batch, (int64_t)hidden, eps, c.st))) return s;
+    return c.back(out, dy, n);
+}
+
+gae_status gae_layernorm_f32_host(const float *input, const float *gamma, const float *beta, size_t n,
+                                  float eps, float *out) {
+    return gae_layernorm_batched_f32_host(input, gamma, beta, n ? 1 : 0, n, eps, out);
+}
+
+gae_status gae_mlp_block_f32_host(const float *input, const float *w1, const float *b1, const float *w2,
+                                  const float *b2, size_t hidden_dim, size_t mlp_dim, size_t tokens,
+                                  float *out) {
+    size_t nx = 0, nh = 0, nw = 0;
+    if (!mul_ok(tokens, hidden_dim, &nx) || !mul_ok(tokens, mlp_dim, &nh) || !mul_ok(hidden_dim, mlp_dim, &nw))
+        return fail(GAE_ERR_INVALID_ARG, "size overflows");
+    if (nx == 0) return GAE_OK;
+    if (!input || !w1 || !b1 || !w2 || !b2 || !out) return fail(GAE_ERR_INVALID_ARG, "NULL host pointer");
+    HostCall c;
+    float *dx, *dw1, *db1, *dw2, *db2, *dh, *dy;
+    gae_status s;
+    if ((s = c.init()) || (s = c.dev(&dx, input, nx)) || (s = c.dev(&dw1, w1, nw)) ||
+        (s = c.dev(&db1, b1, mlp_dim)) || (s = c.dev(&dw2, w2, nw)) || (s = c.dev(&db2, b2, hidden_dim)) ||
+        (s = c.dev(&dh, nullptr, nh)) || (s = c.dev(&dy, nullptr, nx)))
+        return s;
+    const int64_t T = (int64_t)tokens, h = (int64_t)hidden_dim, m = (int64_t)mlp_dim;
+    if ((s = launch_crate_linear(dx, dw1, db1, nullptr, dh, T, m, h, 1, 1, c.st))) return s;
+    if ((s = launch_crate_linear(dh, dw2, db2, nullptr, dy, T, h, m, 1, 0, c.st))) return s;
+    return c.back(out, dy, nx);
+}
+
+gae_status gae_fused_mlp_layernorm_f32_host(const float *input, const float *residual, const float *w1,
+                                            const float *b1, const float *w2, const float *b2,
+                                            const float *gamma, const float *beta, size_t hidden_dim,
+                                            size_t mlp_dim, float eps, size_t tokens, float *out) {
+    size_t nx = 0, nh = 0, nw = 0;
+    if (!mul_ok(tokens, hidden_dim, &nx) || !mul_ok(tokens, mlp_dim, &nh) || !mul_ok(hidden_dim, mlp_dim, &nw))
+        return fail(GAE_ERR_INVALID_ARG, "size overflows");
+    if (nx == 0) return GAE_OK;
+    if (!input || !residual || !w1 || !b1 || !w2 || !b2 || !gamma || !beta || !out)
+        return fail(GAE_ERR_INVALID_ARG, "NULL host pointer");
+    HostCall c;
+    float *dx, *dr, *dw1, *db1, *dw2, *db2, *dg, *dbt, *dh, *dt, *dy;
+    gae_status s;
+    if ((s = c.init()) || (s = c.dev(&dx, input, nx)) || (s = c.dev(&dr, residual, nx)) ||
+        (s = c.dev(&dw1, w1, nw)) || (s = c.dev(&db1, b1, mlp_dim)) || (s = c.dev(&dw2, w2, nw)) ||
+        (s = c.dev(&db2, b2, hidden_dim)) || (s = c.dev(&dg, gamma, hidden_dim)) ||
+        (s = c.dev(&dbt, beta, hidden_dim)) || (s = c.dev(&dh, nullptr, nh)) || (s = c.dev(&dt, nullptr, nx)) ||
+        (s = c.dev(&dy, nullptr, nx)))
+        return s;
+    if ((s = crate_fused_mlp_ln(dx, dr, dw1, db1, dw2, db2, dg, dbt, (int64_t)tokens, (int64_t)hidden_dim,
+                                (int64_t)mlp_dim, eps, dh, dt, dy, c.st)))
+        return s;
+    return c.back(out, dy, nx);
+}
+
+gae_status gae_transformer_block_forward_f32_host(const gae_transformer_block_f32 *b, const float *input,
+                                                  size_t seq_len, float *out) {
+    if (!b) return fail(GAE_ERR_INVALID_ARG, "block is NULL");
+    const size_t h = b->hidden_dim, m = b->mlp_dim;
+    size_t nx = 0, nh = 0, nw = 0, nhh = 0;
+    if (!mul_ok(seq_len, h, &nx) || !mul_ok(seq_len, m, &nh) || !mul_ok(h, m, &nw) || !mul_ok(h, h, &nhh))
+        return fail(GAE_ERR_INVALID_ARG, "size overflows");
+    if (nx == 0) return GAE_OK;
+    if (h == 0 || m == 0) return fail(GAE_ERR_INVALID_ARG, "hidden_dim and mlp_dim must be positive");
+    if (!input || !out || !b->wv || !b->wo || !b->ln1_gamma || !b->ln1_beta || !b->w1 || !b->b1 || !b->w2 ||
+        !b->b2 || !b->ln2_gamma || !b->ln2_beta)
+        return fail(GAE_ERR_INVALID_ARG, "NULL host pointer");
+    HostCall c;
+    float *dx, *dwv, *dwo, *dg1, *db1n, *dw1, *db1, *dw2, *db2, *dg2, *db2n, *dn, *dv, *dr1, *dh, *dt;
+    gae_status s;
+    if ((s = c.init()) || (s = c.dev(&dx, input, nx)) || (s = c.dev(&dwv, b->wv, nhh)) ||
+        (s = c.dev(&dwo, b->wo, nhh)) || (s = c.dev(&dg1, b->ln1_gamma, h)) || (s = c.dev(&db1n, b->ln1_beta, h)) ||
+        (s = c.dev(&dw1, b->w1, nw)) || (s = c.dev(&db1, b->b1, m)) || (s = c.dev(&dw2, b->w2, nw)) ||
+        (s = c.dev(&db2, b->b2, h)) || (s = c.dev(&dg2, b->ln2_gamma, h)) || (s = c.dev(&db2n, b->ln2_beta, h)) ||
+        (s = c.dev(&dn, nullptr, nx)) || (s = c.dev(&dv, nullptr, nx)) || (s = c.dev(&dr1, nullptr, nx)) ||
+        (s = c.dev(&dh, nullptr, nh)) || (s = c.dev(&dt, nullptr, nx)))
+        return s;
+    const int64_t T = (int64_t)seq_len, H = (int64_t)h, M = (int64_t)m;
+    // transformer.rs:97-116, every token independently: LN1 -> Wv -> Wo + x ->
+    // LN2(MLP(r1) + r1).  dn is reused for the final output.
+    if ((s = launch_crate_layernorm(dx, dg1, db1n, dn, T, H, b->eps, c.st))) return s;
+    if ((s = launch_crate_linear(dn, dwv, nullptr, nullptr, dv, T, H, H, 0, 0, c.st))) return s;
+    if ((s = launch_crate_linear(dv, dwo, nullptr, dx, dr1, T, H, H, 0, 2, c.st))) return s;
+    if ((s = crate_fused_mlp_ln(dr1, dr1, dw1, db1, dw2, db2, dg2, db2n, T, H, M, b->eps, dh, dt, dn, c.st)))
+        return s;
+    return c.back(out, dn, nx);
+}
 }  // extern "C"
 
 // ====================================================================
@@ -977,21 +1180,44 @@ static __device__ __align__(256) unsigned char g_layer_static_ws[kStaticLayerWsB
 constexpr int kStaticMaxDevices = 64;
 std::mutex g_static_ws_mu;
 void *g_static_ws_ptr[kStaticMaxDevices] = {};
+CUcontext g_static_ws_ctx[kStaticMaxDevices] = {};
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<CtxGetCurrentFn>(p);
+    }();
+    return fn;
+}
 
 // Device address of the array on the current device.  Host code may not use
 // the array's name as a pointer (it is only a host-side stand-in), so the
-// address is looked up once per device, with that device current.
+// address is looked up once per device, with that device current.  The
+// context it was looked up in is kept beside it: after a cudaDeviceReset (a
+// new primary context, the module loaded again, perhaps elsewhere) the
+// address is looked up afresh instead of reusing a stale one.
 gae_status static_ws_address(void **out) {
     int dev = 0;
     GAE_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kStaticMaxDevices)
         return fail(GAE_ERR_UNSUPPORTED, "device index %d beyond %d", dev, kStaticMaxDevices);
+    CtxGetCurrentFn get_ctx = ctx_get_current_fn();
+    if (!get_ctx) return fail(GAE_ERR_CUDA, "cuCtxGetCurrent is unavailable");
+    CUcontext ctx = nullptr;
+    get_ctx(&ctx);
     std::lock_guard<std::mutex> lock(g_static_ws_mu);
-    if (!g_static_ws_ptr[dev]) {
+    if (!ctx || !g_static_ws_ptr[dev] || g_static_ws_ctx[dev] != ctx) {
         void *p = nullptr;
-        GAE_CUDA_TRY(cudaGetSymbolAddress(&p, g_layer_static_ws));
+        GAE_CUDA_TRY(cudaGetSymbolAddress(&p, g_layer_static_ws));  // also makes the context current
         if (!p) return fail(GAE_ERR_CUDA, "cudaGetSymbolAddress returned NULL");
+        if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return fail(GAE_ERR_CUDA, "no current CUDA context");
         g_static_ws_ptr[dev] = p;
+        g_static_ws_ctx[dev] = ctx;
     }
     *out = g_static_ws_ptr[dev];
     return GAE_OK;
@@ -1004,7 +1230,11 @@ extern "C" gae_status gae_layer_fwd_static(const gae_layer_args *a, const gae_la
     if (!a) return fail(GAE_ERR_INVALID_ARG, "args is NULL");
     if (a->batch < 1 || a->seq < 1 || a->d_model < 1 || a->d_ff < 1)
         return fail(GAE_ERR_INVALID_ARG, "invalid layer shape");
-    const size_t need = layer_ws(a->batch * a->seq, a->d_model, a->d_ff).total;
+    if (a->batch > ((int64_t)1 << 31) / a->seq)
+        return fail(GAE_ERR_INVALID_ARG, "batch*seq beyond 2^31 tokens");
+    const LayerWs L = layer_ws(a->batch * a->seq, a->d_model, a->d_ff);
+    if (!L.ok) return fail(GAE_ERR_INVALID_ARG, "layer shape too large (workspace size overflows)");
+    const size_t need = L.total;
     if (need > kStaticLayerWsBytes)
         return fail(GAE_ERR_UNSUPPORTED,
                     "gae_layer_fwd_static: this shape needs %zu bytes of workspace, above the "

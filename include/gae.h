@@ -11,8 +11,8 @@
  *
  * Each declaration names the reference interface it replaces
  * (RegularJoe-CEO/Geodesic-Attention-Engine-GAE-, path:line inside that
- * project).  The reference crate `ate` panics on bad input; the Rust binding
- * shown in INTEGRATION.md turns a non-GAE_OK status back into a panic.
+ * project).  The reference crate `ate` panics on bad input; a Rust binding
+ * keeps those semantics by turning a non-GAE_OK status back into a panic.
  */
 #ifndef GAE_H_
 #define GAE_H_
@@ -89,6 +89,74 @@ GAE_API gae_status gae_waller_operator_parallel_f32_host(const float *q, const f
 GAE_API gae_status gae_standard_attention_f32_host(const float *q, const float *k, const float *v,
                                            size_t seq_len, size_t head_dim, float scale,
                                            int causal, float *out);
+
+/* ------------------------------------------------------------------------
+ * The crate's fp32 layer functions, computed in the crate's own order.
+ * Each output element is one sequential f32 sum in increasing index order
+ * with no fused multiply-add, and LayerNorm uses the crate's single-pass
+ * Welford statistics, so sums, statistics and normalisation match the
+ * crate's f32 results bit for bit; GELU's tanh may differ in the last place.
+ * Host entry points take host slices as the crate does and are synchronous
+ * (they allocate device memory for the call).  `tokens` rows are processed
+ * independently; the crate's own call is tokens = 1.  Any widths.
+ * ---------------------------------------------------------------------- */
+
+/* replaces ate::layernorm, rust_src/src/layernorm.rs:6-17 (one row of n) */
+GAE_API gae_status gae_layernorm_f32_host(const float *input, const float *gamma, const float *beta,
+                                          size_t n, float eps, float *out);
+
+/* replaces ate::layernorm_batched, rust_src/src/layernorm.rs:20-47 */
+GAE_API gae_status gae_layernorm_batched_f32_host(const float *input, const float *gamma,
+                                                  const float *beta, size_t batch, size_t hidden,
+                                                  float eps, float *out);
+
+/* replaces ate::mlp_block, rust_src/src/mlp.rs:7-36: gelu(x @ W1 + b1) @ W2 + b2,
+ * W1 [hidden_dim, mlp_dim], W2 [mlp_dim, hidden_dim] row-major (the crate's
+ * layouts); input/out [tokens, hidden_dim]. */
+GAE_API gae_status gae_mlp_block_f32_host(const float *input, const float *w1, const float *b1,
+                                          const float *w2, const float *b2, size_t hidden_dim,
+                                          size_t mlp_dim, size_t tokens, float *out);
+
+/* replaces ate::fused_mlp_layernorm, rust_src/src/mlp.rs:39-73:
+ * LayerNorm(mlp_block(input) + residual) per token. */
+GAE_API gae_status gae_fused_mlp_layernorm_f32_host(const float *input, const float *residual,
+                                                    const float *w1, const float *b1,
+                                                    const float *w2, const float *b2,
+                                                    const float *gamma, const float *beta,
+                                                    size_t hidden_dim, size_t mlp_dim, float eps,
+                                                    size_t tokens, float *out);
+
+/* The weights and config of ate::TransformerBlock (rust_src/src/transformer.rs:
+ * 9-33): wq/wk/wv/wo [hidden, hidden] as W[out, in] (wq and wk are unused by
+ * the crate's forward and may be NULL), w1 [hidden, mlp], w2 [mlp, hidden]. */
+typedef struct {
+    const float *wq, *wk, *wv, *wo;
+    const float *ln1_gamma, *ln1_beta;
+    const float *w1, *b1;
+    const float *w2, *b2;
+    const float *ln2_gamma, *ln2_beta;
+    size_t hidden_dim, num_heads, head_dim, mlp_dim;
+    float eps;
+} gae_transformer_block_f32;
+
+/* replaces ate::TransformerBlock::forward, rust_src/src/transformer.rs:87-120:
+ * per token LN1 -> Wv -> Wo + input -> fused_mlp_layernorm(r1, r1) (the
+ * crate's forward has no cross-token attention).  input/out [seq_len, hidden]. */
+GAE_API gae_status gae_transformer_block_forward_f32_host(const gae_transformer_block_f32 *block,
+                                                          const float *input, size_t seq_len,
+                                                          float *out);
+
+/* Device-pointer forms of the two kernels above (stream-ordered):
+ * y[M, N] = epi(init + sum_j x[M, j] * W(j, n)), init = bias[n] or 0 (bias
+ * NULL), W(j, n) = w[j*N + n] when w_in_major (the crate's W1/W2) else
+ * w[n*K + j] (the crate's matvec, transformer.rs:124-134); epilogue 0 none,
+ * 1 GELU (activations.rs:5-7), 2 + res[M, N].  And the Welford LayerNorm of
+ * rows [rows, d]. */
+GAE_API gae_status gae_crate_linear_f32(const float *x, const float *w, const float *bias,
+                                        const float *res, float *y, int64_t M, int64_t N, int64_t K,
+                                        int w_in_major, int epilogue, void *stream);
+GAE_API gae_status gae_crate_layernorm_f32(const float *x, const float *gamma, const float *beta,
+                                           float *y, int64_t rows, int64_t d, float eps, void *stream);
 
 /* ------------------------------------------------------------------------
  * Device-pointer attention (the reference's CUDA Waller kernels:
@@ -282,7 +350,8 @@ GAE_API gae_status gae_layer_stack_fwd(const gae_layer_args *args, const gae_lay
  * gae_layer_workspace_bytes exceeds 32 MiB (e.g. about 1980 tokens at GPT-2
  * small widths) return GAE_ERR_UNSUPPORTED.  Nothing is allocated; the first
  * call on a device looks up the array's device address (cudaGetSymbolAddress),
- * so make that first call before any stream capture.  Every call shares the one
+ * so make that first call before any stream capture; after a cudaDeviceReset
+ * the next call looks it up again (make that call outside capture too).  Every call shares the one
  * array, which keeps the previous call's contents (the layer writes every
  * workspace byte it reads, so nothing needs clearing); calls that overlap on
  * the GPU (other streams, other threads) race on it and must be serialised by

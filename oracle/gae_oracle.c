@@ -539,6 +539,16 @@ int ora_num_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP thread count of later parallel regions (the CPU baseline
+ * uses every host core whatever OMP_NUM_THREADS a launcher exported). */
+void ora_set_num_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------------ */
 /* Fused "symphony" layer (cuda_src/waller_fused_layer.cu:64-247): one token  */
 /* through identity-Q int8 causal attention, a gated residual, RMSNorm, an    */

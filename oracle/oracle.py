@@ -17,6 +17,14 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "build", "libgae_oracle.so")
+
+
+def reference_root() -> str:
+    """Root of the reference checkout: $GAE_REFERENCE_ROOT, else a
+    `reference/` directory beside this repository.  It exists only where the
+    reference is checked out (never on a GPU box); callers test for it."""
+    return os.environ.get("GAE_REFERENCE_ROOT") or os.path.join(
+        os.path.dirname(os.path.dirname(_HERE)), "reference")
 _lib = None
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
@@ -28,10 +36,9 @@ _sz = C.c_size_t
 def build() -> str:
     """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
-    ref_src = os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference", "cuda_src",
-                           "waller_fused_layer.cu")
-    if os.path.exists(ref_src):  # the reference tree exists only where it is checked out
-        subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+    root = reference_root()
+    if os.path.exists(os.path.join(root, "cuda_src", "waller_fused_layer.cu")):
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={os.path.abspath(root)}"], check=True)
     return _LIB_PATH
 
 
@@ -148,6 +155,7 @@ def lib():
     L.ora_symphony_layer.argtypes = [_f32p, _i8p, _i8p, _f32p, _f32p, _f32p, _f32p, _sz, _sz,
                                      _f32p, C.c_int, _f32p]
     L.ora_num_threads.restype = C.c_int
+    L.ora_set_num_threads.argtypes = [C.c_int]
     _lib = L
     return L
 
@@ -346,6 +354,14 @@ def gpt2_layer(x, B, S, D, nh, F, eps, w, round_bf16=True):
 
 def num_threads() -> int:
     return lib().ora_num_threads()
+
+
+def use_all_cores() -> int:
+    """Runs later oracle parallel regions on every core this process may use
+    (launchers such as torchrun export OMP_NUM_THREADS=1); returns the count."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    lib().ora_set_num_threads(n)
+    return num_threads()
 
 
 def symphony_layer(x, k, v, w_up, w_down, n1, n2, tuning, act=0):

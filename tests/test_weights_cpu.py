@@ -3,6 +3,7 @@ naming, [in, out] -> [out, in] transposition, size checks, partial files.
 The last test loads the reference's own `layer_weights/` biases where the
 reference tree is checked out beside this repository (skipped elsewhere)."""
 import os
+import sys
 
 import numpy as np
 import pytest
@@ -10,7 +11,10 @@ import pytest
 torch = pytest.importorskip("torch")
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_WEIGHTS = os.path.join(os.path.dirname(ROOT), "reference", "layer_weights")
+sys.path.insert(0, ROOT)
+from oracle.oracle import reference_root  # noqa: E402
+
+REF_WEIGHTS = os.path.join(reference_root(), "layer_weights")
 
 
 def test_load_weights_transposes_and_reports(gae, tmp_path):
