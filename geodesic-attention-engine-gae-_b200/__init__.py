@@ -134,6 +134,7 @@ def lib():
     L.gae_crate_layernorm_f32.argtypes = [vp, vp, vp, vp, i64, i64, C.c_float, vp]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     L.gae_debug_wait_timeout.argtypes = [C.c_uint64, vp]
+    L.gae_debug_attn_int8_logits.argtypes = [C.POINTER(AttnInt8Args), vp, vp]
     _lib = L
     return L
 
@@ -329,8 +330,10 @@ def quantize_rows_int8(x, stream=None):
 
 
 def attention_int8(q, k, q_scale, k_scale, v, *, causal=False, scale=None, out=None,
-                   return_lse=False, stream=None):
-    """INT8 attention: q, k int8 [BH, N, D] + fp32 row scales [BH, N]; v bf16 [BH, N, D]."""
+                   return_lse=False, stream=None, logits_out=None):
+    """INT8 attention: q, k int8 [BH, N, D] + fp32 row scales [BH, N]; v bf16 [BH, N, D].
+    logits_out (diagnostics, int32 [BH, N, N] on the device): the same kernel
+    also writes the exact int32 logits it computed (gae_debug_attn_int8_logits)."""
     torch = _torch()
     BH, N, D = q.shape
     if out is None:
@@ -346,7 +349,13 @@ def attention_int8(q, k, q_scale, k_scale, v, *, causal=False, scale=None, out=N
     a.batch_heads, a.seq, a.head_dim = BH, N, D
     a.causal = 1 if causal else 0
     a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
-    _check(lib().gae_attn_int8_fwd(C.byref(a), _stream_ptr(stream)))
+    if logits_out is not None:
+        if tuple(logits_out.shape) != (BH, N, N) or logits_out.dtype != torch.int32 or \
+                not logits_out.is_contiguous():
+            raise GAEError(1, "attention_int8: logits_out must be contiguous int32 [BH, N, N]")
+        _check(lib().gae_debug_attn_int8_logits(C.byref(a), logits_out.data_ptr(), _stream_ptr(stream)))
+    else:
+        _check(lib().gae_attn_int8_fwd(C.byref(a), _stream_ptr(stream)))
     return (out, lse) if return_lse else out
 
 

@@ -55,6 +55,10 @@ struct AttnParams {
     int causal;
     float scale_log2;  // scale * log2(e)
     int64_t q_offset, kv_offset;
+    // int8 mode, diagnostics (the kDump instantiation): every softmax thread
+    // also writes the exact int32 logits it read from TMEM, [B*H, Nq, Nkv]
+    // (tiles wholly above the causal diagonal are never computed).
+    int32_t *logits_dump;
 };
 
 // Optional cycle-stamp trace of one CTA (diagnostics; see gae_debug.h).  When
@@ -171,7 +175,10 @@ __device__ __forceinline__ constexpr bool use_poly_exp(int e) {
     return kPeriod > 0 && (e % (kPeriod > 0 ? kPeriod : 1)) == kPeriod - 1;
 }
 
-template <int D, int kMode>
+// kDump (int8 mode, diagnostics): the same kernel also writes the int32
+// logits it reads from TMEM to p.logits_dump; a separate instantiation so
+// the production kernel carries none of its registers.
+template <int D, int kMode, bool kDump = false>
 __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
     using Cfg = AttnCfg<D, kMode>;
     constexpr bool kBF16 = kMode != kModeF16;  // P and O are bf16 in bf16 and int8 modes
@@ -520,6 +527,18 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 tmem_ld32(tS + 96, r3);
                 tmem_wait_ld();
                 if constexpr (Cfg::kInt8) {
+                    if (kDump && q_local < p.Nq) {
+                        int32_t *dst = p.logits_dump + ((int64_t)bh * p.Nq + q_local) * p.Nkv +
+                                       (int64_t)j * Cfg::kBlockN;
+                        const int nk = min(Cfg::kBlockN, p.Nkv - j * Cfg::kBlockN);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {  // constant register indices
+                            if (e < nk) dst[e] = (int32_t)r0[e];
+                            if (32 + e < nk) dst[32 + e] = (int32_t)r1[e];
+                            if (64 + e < nk) dst[64 + e] = (int32_t)r2[e];
+                            if (96 + e < nk) dst[96 + e] = (int32_t)r3[e];
+                        }
+                    }
                     // Exact int32 logits times the keys' dequantisation scales.  The
                     // scales arrived with K_j; its slot is released only after both
                     // softmax groups finished tile j.

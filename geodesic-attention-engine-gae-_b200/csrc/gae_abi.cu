@@ -122,9 +122,9 @@ gae_status make_map_2d_f32(CUtensorMap *m, const void *ptr, int64_t n, int64_t r
     return GAE_OK;
 }
 
-template <int D, int kMode>
+template <int D, int kMode, bool kDump = false>
 gae_status launch_tc(const gae::AttnParams &p, dim3 grid, cudaStream_t st) {
-    auto kern = gae::attn_fwd_sm100_kernel<D, kMode>;
+    auto kern = gae::attn_fwd_sm100_kernel<D, kMode, kDump>;
     constexpr int smem = gae::AttnCfg<D, kMode>::kSmemBytes;
     gae_status s = set_smem(kern, smem);
     if (s != GAE_OK) return s;
@@ -325,7 +325,7 @@ gae_status launch_attn_bwd(const gae_attn_bwd_args *a, cudaStream_t st) {
     return GAE_OK;
 }
 
-gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st) {
+gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st, int32_t *logits_dump = nullptr) {
     const int64_t D = a->head_dim, BH = a->batch_heads, N = a->seq;
     if (D != 128) return fail(GAE_ERR_UNSUPPORTED, "int8 attention supports head_dim 128, got %lld", (long long)D);
     if (BH > 65535) return fail(GAE_ERR_UNSUPPORTED, "batch_heads > 65535");
@@ -353,7 +353,9 @@ gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st) {
     p.scale_log2 = a->scale * 1.4426950408889634f;
     const int64_t units = (int64_t)p.n_qpairs * BH;
     p.head_major = 1;
+    p.logits_dump = logits_dump;
     dim3 grid((unsigned)units);  // one CTA per unit (measured faster than persistent for int8)
+    if (logits_dump) return launch_tc<128, gae::kModeInt8, true>(p, grid, st);
     return launch_tc<128, gae::kModeInt8>(p, grid, st);
 }
 
@@ -838,6 +840,14 @@ __global__ void wait_timeout_probe_kernel(uint64_t timeout_ns, unsigned site) {
     if (threadIdx.x == 0) mbar_wait_for(smem_u32(&bar), 0, site, &abort_flag, timeout_ns);
 }
 }  // namespace gae
+
+extern "C" gae_status gae_debug_attn_int8_logits(const gae_attn_int8_args *a, int32_t *logits, void *stream) {
+    if (!a || !logits) return fail(GAE_ERR_INVALID_ARG, "args or logits NULL");
+    if (a->batch_heads < 1 || a->seq < 0 || a->head_dim < 1)
+        return fail(GAE_ERR_INVALID_ARG, "invalid int8 attention shape");
+    if (a->seq == 0) return GAE_OK;
+    return launch_attn_int8(a, static_cast<cudaStream_t>(stream), logits);
+}
 
 extern "C" gae_status gae_debug_wait_timeout(uint64_t timeout_ns, void *stream) {
     if (timeout_ns > 1000000000ull) return fail(GAE_ERR_INVALID_ARG, "timeout above 1 s");

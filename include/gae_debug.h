@@ -29,6 +29,16 @@ extern "C" {
  * from the heaviest query block (x = 0 is the last 256 query rows). */
 GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
 
+/* Runs the INT8 attention kernel of gae_attn_int8_fwd (same arguments, same
+ * outputs) and has it also write the exact int32 logits q_i . k_j that its
+ * softmax threads read back from the tensor memory, logits int32
+ * [batch_heads, seq, seq] (tiles wholly above the causal diagonal are not
+ * computed and are left as they were).  Pins the bit-exact int32 QK^T of
+ * the attention kernel itself (the reference's dot_int8,
+ * cuda_src/waller_operator_int8.cu:13-24). */
+GAE_API gae_status gae_debug_attn_int8_logits(const gae_attn_int8_args *args, int32_t *logits,
+                                              void *stream);
+
 /* Exercises the library's bounded device-side wait: launches one thread that
  * waits on an mbarrier nothing will complete, with a limit of timeout_ns
  * (at most 1 s).  The wait gives up, records site 0x901 and the kernel exits

@@ -32,6 +32,33 @@ def test_config1_f32_host_dropin(gae, ora, causal):
     assert np.linalg.norm(out - ref) / np.linalg.norm(ref) <= 1e-5
     rows, gold = load_golden("config1_causal" if causal else "config1_noncausal")
     assert rel_scale(out[rows], gold) <= 1e-5
+    # the elementwise-relative form (floor 1e-3 of the largest output)
+    assert elementwise_rel(out, ref) <= 1e-3
+
+
+def elementwise_rel(a, b):
+    """max |a - b| / max(|b|, 1e-3 max|b|): the elementwise-relative fp32
+    metric (tighter than rel_scale on small outputs)."""
+    b_abs = np.abs(b)
+    return float((np.abs(a - b) / np.maximum(b_abs, 1e-3 * b_abs.max())).max())
+
+
+@pytest.mark.parametrize("n,d,causal", [(1024, 64, True), (1024, 64, False), (333, 40, True),
+                                        (96, 256, False)])
+def test_standard_attention_against_oracle(gae, ora, n, d, causal):
+    """ate::standard_attention (standard_attention.rs:13-65) through
+    gae_standard_attention_f32_host against the oracle's restatement of the
+    materialised N x N form (not against the library's own Waller path):
+    1e-5 of the output's scale and 1e-5 relative L2; the elementwise-relative
+    error is bounded too."""
+    rng = np.random.default_rng(n + d)
+    q, k, v = (rng.standard_normal(n * d).astype(np.float32) for _ in range(3))
+    scale = 1.0 / math.sqrt(d)
+    got = gae.standard_attention(q, k, v, n, d, scale, causal=causal)
+    ref = ora.standard_attention(q, k, v, n, d, scale, causal=causal)
+    assert rel_scale(got, ref) <= 1e-5
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= 1e-5
+    assert elementwise_rel(got, ref) <= 1e-3
 
 
 def test_reference_kats_on_gpu(gae):
