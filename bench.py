@@ -596,7 +596,11 @@ def main():
     if is_ring and w.get("sp") == "ulysses":
         launches_per_step = 1
     else:
-        launches_per_step = (4 + 4 * (world - 1)) if is_ring else (7 * w["layers"] if is_gpt2 else 1)
+        # the C-ABI ring on rank 0: 1 launch at P=1; otherwise 9 re-deal
+        # copies, 1 fill, 2 block launches + 2 merges at step 0 and 1 + 1 per
+        # further step, 4 copies of the output re-deal
+        launches_per_step = ((1 if world == 1 else 18 + 2 * (world - 1)) if is_ring
+                             else (7 * w["layers"] if is_gpt2 else 1))
     if is_sym:
         launches_per_step = 3  # prep, attention, post
     if is_bwd:

@@ -132,6 +132,13 @@ def lib():
     L.gae_transformer_block_forward_f32_host.argtypes = [vp, vp, sz, vp]
     L.gae_crate_linear_f32.argtypes = [vp, vp, vp, vp, vp, i64, i64, i64, C.c_int, C.c_int, vp]
     L.gae_crate_layernorm_f32.argtypes = [vp, vp, vp, vp, i64, i64, C.c_float, vp]
+    L.gae_ring_unique_id.argtypes = [vp]
+    L.gae_ring_ctx_create.argtypes = [vp, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_void_p)]
+    L.gae_ring_ctx_create_from_comm.argtypes = [vp, C.c_double, C.POINTER(C.c_void_p)]
+    L.gae_ring_attn_fwd.argtypes = [vp, C.POINTER(AttnArgs), C.c_int, vp]
+    L.gae_ring_ctx_destroy.argtypes = [vp]
+    L.gae_debug_ring_plan.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, i64, vp,
+                                      C.POINTER(C.c_int)]
     L.gae_debug_attn_trace.argtypes = [vp, C.c_int]
     L.gae_debug_wait_timeout.argtypes = [C.c_uint64, vp]
     L.gae_debug_attn_int8_logits.argtypes = [C.POINTER(AttnInt8Args), vp, vp]
@@ -209,10 +216,18 @@ def attention(q, k, v, *, causal: bool = False, scale: float | None = None, q_of
         lse = torch.empty((B, H, Nq), dtype=torch.float32, device=q.device)
     if lse is not None and (not lse.is_contiguous() or lse.dtype != torch.float32):
         raise GAEError(1, "lse must be a contiguous fp32 tensor [B, H, Nq]")
+    a = _attn_args(q, k, v, out, lse, causal, scale, q_offset, kv_offset)
+    _check(lib().gae_attn_fwd(C.byref(a), _stream_ptr(stream)))
+    return (out, lse) if return_lse else out
+
+
+def _attn_args(q, k, v, out, lse, causal, scale, q_offset=0, kv_offset=0):
+    """gae_attn_args for device tensors [B, H, N, D] (strided views)."""
+    B, H, Nq, D = q.shape
     a = AttnArgs()
     a.q, a.k, a.v, a.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
     a.lse = lse.data_ptr() if lse is not None else None
-    a.batch, a.heads, a.seq_q, a.seq_kv, a.head_dim = B, H, Nq, Nkv, D
+    a.batch, a.heads, a.seq_q, a.seq_kv, a.head_dim = B, H, Nq, k.shape[2], D
     a.q_stride[:] = _bhsd(q, "q")
     a.k_stride[:] = _bhsd(k, "k")
     a.v_stride[:] = _bhsd(v, "v")
@@ -221,8 +236,7 @@ def attention(q, k, v, *, causal: bool = False, scale: float | None = None, q_of
     a.causal = 1 if causal else 0
     a.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
     a.q_offset, a.kv_offset = int(q_offset), int(kv_offset)
-    _check(lib().gae_attn_fwd(C.byref(a), _stream_ptr(stream)))
-    return (out, lse) if return_lse else out
+    return a
 
 
 def attention_backward(q, k, v, out, dout, lse, *, causal: bool = False, scale: float | None = None,

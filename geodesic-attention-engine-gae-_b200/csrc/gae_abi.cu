@@ -786,6 +786,8 @@ gae_status crate_fused_mlp_ln(const float *x, const float *res, const float *w1,
 bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
 }  // namespace
 
+#include "ring.cuh"
+
 // ==================================================================== C ABI
 extern "C" {
 
@@ -1168,6 +1170,122 @@ gae_status gae_transformer_block_forward_f32_host(const gae_transformer_block_f3
     if ((s = crate_fused_mlp_ln(dr1, dr1, dw1, db1, dw2, db2, dg2, db2n, T, H, M, b->eps, dh, dt, dn, c.st)))
         return s;
     return c.back(out, dn, nx);
+}
+
+// ------------------------------------------------- sequence-parallel ring
+gae_status gae_ring_unique_id(void *unique_id) {
+    if (!unique_id) return fail(GAE_ERR_INVALID_ARG, "unique_id is NULL");
+    const NcclApi *nc = nccl_api();
+    if (!nc) return fail(GAE_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    const ncclResult_t r = nc->GetUniqueId(&id);
+    if (r != ncclSuccess) return fail(GAE_ERR_COMM, "ncclGetUniqueId: %s", nc->GetErrorString(r));
+    static_assert(sizeof(ncclUniqueId) == GAE_RING_UNIQUE_ID_BYTES, "unique id size");
+    memcpy(unique_id, &id, sizeof(id));
+    return GAE_OK;
+}
+
+gae_status gae_ring_ctx_create(const void *unique_id, int rank, int world, double timeout_s, gae_ring_ctx **out) {
+    if (!out || !unique_id) return fail(GAE_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    if (world < 1 || rank < 0 || rank >= world) return fail(GAE_ERR_INVALID_ARG, "rank %d of world %d", rank, world);
+    const NcclApi *nc = nccl_api();
+    if (!nc) return fail(GAE_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    gae_ring_ctx *c = new gae_ring_ctx();
+    c->nc = nc;
+    c->rank = rank;
+    c->world = world;
+    c->timeout_s = timeout_s;
+    gae_status s = ring_ctx_init_common(c);
+    if (s == GAE_OK) {
+        ncclUniqueId id;
+        memcpy(&id, unique_id, sizeof(id));
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;  // every wait is bounded by the timeout
+        const ncclResult_t r = nc->CommInitRankConfig(&c->comm, world, id, rank, &cfg);
+        c->owns_comm = true;
+        if (r != ncclSuccess && r != ncclInProgress)
+            s = fail(GAE_ERR_COMM, "ncclCommInitRankConfig: %s", nc->GetErrorString(r));
+        else
+            s = nccl_settle(c, r, "joining the communicator");
+    }
+    if (s != GAE_OK) {
+        const gae_status keep = g_err_status;
+        char msg[sizeof g_err];
+        memcpy(msg, g_err, sizeof msg);
+        ring_ctx_release(c);
+        g_err_status = keep;
+        memcpy(g_err, msg, sizeof msg);
+        return s;
+    }
+    *out = c;
+    return GAE_OK;
+}
+
+gae_status gae_ring_ctx_create_from_comm(void *nccl_comm, double timeout_s, gae_ring_ctx **out) {
+    if (!out || !nccl_comm) return fail(GAE_ERR_INVALID_ARG, "NULL argument");
+    *out = nullptr;
+    const NcclApi *nc = nccl_api();
+    if (!nc) return fail(GAE_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    gae_ring_ctx *c = new gae_ring_ctx();
+    c->nc = nc;
+    c->comm = static_cast<ncclComm_t>(nccl_comm);
+    c->owns_comm = false;
+    c->timeout_s = timeout_s;
+    gae_status s = ring_ctx_init_common(c);
+    if (s == GAE_OK && (nc->CommCount(c->comm, &c->world) != ncclSuccess ||
+                        nc->CommUserRank(c->comm, &c->rank) != ncclSuccess))
+        s = fail(GAE_ERR_COMM, "the communicator reports no rank/size");
+    if (s != GAE_OK) {
+        ring_ctx_release(c);
+        return s;
+    }
+    *out = c;
+    return GAE_OK;
+}
+
+gae_status gae_ring_ctx_destroy(gae_ring_ctx *ctx) {
+    if (ctx) ring_ctx_release(ctx);
+    return GAE_OK;
+}
+
+gae_status gae_ring_attn_fwd(gae_ring_ctx *ctx, const gae_attn_args *a, int balance, void *stream) {
+    int zig = 0;
+    gae_status s = ring_check_args(ctx, a, balance, &zig);
+    if (s != GAE_OK) return s;
+    if (a->seq_q == 0) return GAE_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int dev = -1;
+    GAE_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev != ctx->device) return fail(GAE_ERR_INVALID_ARG, "current device %d is not the context's %d", dev, ctx->device);
+    if (ctx->world == 1) return launch_attn_tc(a, st);  // the whole sequence is here: one launch
+    if (ctx->comm) {
+        ncclResult_t as = ncclSuccess;
+        if (ctx->nc->CommGetAsyncError(ctx->comm, &as) != ncclSuccess || (as != ncclSuccess && as != ncclInProgress))
+            return ring_fail(ctx, GAE_ERR_COMM, "communicator", ctx->nc->GetErrorString(as));
+    }
+    s = a->dtype == GAE_DTYPE_BF16 ? ring_run<__nv_bfloat16>(ctx, a, zig, st) : ring_run<__half>(ctx, a, zig, st);
+    if (s != GAE_OK) return s;
+    if (ctx->timeout_s > 0) {
+        GAE_CUDA_TRY(cudaEventRecord(ctx->ev_done, st));
+        return ring_wait_event(ctx, ctx->ev_done, "waiting for the ring to finish");
+    }
+    return GAE_OK;
+}
+
+gae_status gae_debug_ring_plan(int rank, int world, int step, int causal, int zigzag, int64_t shard_len,
+                               int64_t *ops, int *n_ops) {
+    if (!ops || !n_ops || world < 1 || rank < 0 || rank >= world || step < 0 || step >= world || shard_len < 0)
+        return fail(GAE_ERR_INVALID_ARG, "invalid ring plan query");
+    RingOp o[2];
+    const int n = ring_plan(rank, world, step, causal, zigzag, shard_len, o);
+    for (int i = 0; i < n; ++i) {
+        const int64_t v[7] = {o[i].q_row0, o[i].q_rows, o[i].kv_row0, o[i].kv_rows, o[i].causal, o[i].q_pos,
+                              o[i].kv_pos};
+        memcpy(ops + 7 * i, v, sizeof v);
+    }
+    *n_ops = n;
+    return GAE_OK;
 }
 }  // extern "C"
 

@@ -26,9 +26,14 @@ other ranks' exchange fail (an error from the backend or the process group's
 timeout); the driver raises GAEError(GAE_ERR_COMM) naming the step.  The
 timeout is the process group's (init_process_group(timeout=...)).
 
-`attend` and `merge` are injectable so that the host logic can be exercised on
-CPU ranks (gloo) in tests; the product path uses the CUDA kernels and fails
-loudly without them.
+Two host paths with one algorithm.  On CUDA tensors with no injected
+`attend`/`merge`, ring_attention is a thin caller of the library's C ABI
+(gae_ring_ctx_create / gae_ring_attn_fwd): the re-deal, the K/V rotation
+over NCCL send/recv, the attention launches and the merges run in libgae.so
+(one communicator per process group, created on first use from a unique id
+broadcast over the group).  With `attend` and `merge` injected (CPU gloo
+tests), the same plan runs here in Python over torch.distributed.  The
+product path fails loudly without the CUDA library.
 """
 from __future__ import annotations
 
@@ -122,6 +127,62 @@ def _redeal(x, rank, P, group, to_zigzag: bool):
     return out
 
 
+_CTX = {}
+RING_TIMEOUT_S = 120.0  # bound on every wait of the C-ABI ring (communicator and completion)
+
+
+def _group_key(group):
+    return (None if group is None else id(group), __import__("torch").cuda.current_device())
+
+
+def ring_context(group=None, timeout_s: float = RING_TIMEOUT_S):
+    """The C-ABI ring context of `group` on the current device (created on
+    first use, collectively: rank 0 of the group makes an NCCL unique id and
+    broadcasts it over the group)."""
+    import ctypes as C
+    from . import lib, _check
+    key = _group_key(group)
+    if key in _CTX:
+        return _CTX[key]
+    P = dist.get_world_size(group) if dist.is_initialized() else 1
+    r = dist.get_rank(group) if dist.is_initialized() else 0
+    uid = (C.c_ubyte * 128)()
+    if r == 0:
+        _check(lib().gae_ring_unique_id(uid))
+    if P > 1:
+        obj = [bytes(uid)]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        try:
+            dist.broadcast_object_list(obj, src=src, group=group)
+        except Exception as e:
+            raise _comm_error("sharing the ring's NCCL id", e) from e
+        C.memmove(uid, obj[0], 128)
+    ctx = C.c_void_p()
+    _check(lib().gae_ring_ctx_create(uid, r, P, float(timeout_s), C.byref(ctx)))
+    _CTX[key] = ctx
+    return ctx
+
+
+def release_contexts():
+    """Destroys every C-ABI ring context of this process (collective over
+    each context's ranks)."""
+    from . import lib
+    for key in list(_CTX):
+        lib().gae_ring_ctx_destroy(_CTX.pop(key))
+
+
+def _ring_attention_native(q, k, v, group, causal, balance, scale, return_lse):
+    import ctypes as C
+    from . import lib, _check, _attn_args, _stream_ptr
+    B, H, S, D = q.shape
+    out = torch.empty_like(q)
+    lse = torch.empty((B, H, S), dtype=torch.float32, device=q.device) if return_lse else None
+    a = _attn_args(q, k, v, out, lse, causal, scale)
+    bal = 0 if balance == "zigzag" else 1
+    _check(lib().gae_ring_attn_fwd(ring_context(group), C.byref(a), bal, _stream_ptr(None)))
+    return (out, lse) if return_lse else out
+
+
 def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "zigzag",
                    scale: float | None = None, return_lse: bool = False, attend=None,
                    merge=None):
@@ -130,6 +191,15 @@ def ring_attention(q, k, v, *, group=None, causal: bool = True, balance: str = "
     q, k, v: this rank's contiguous shard [B, H, S, D].  Returns the output
     shard (dtype of q) and, with return_lse, the fp32 log-sum-exp [B, H, S].
     """
+    if balance not in ("zigzag", "contiguous"):
+        raise ValueError(f"unknown balance {balance!r}")
+    if attend is None and merge is None and q.is_cuda:
+        if k.shape != q.shape or v.shape != q.shape:
+            raise ValueError("ring_attention: q, k, v shards must have the same shape")
+        if causal and balance == "zigzag" and q.shape[2] % 2 and \
+                (dist.get_world_size(group) if dist.is_initialized() else 1) > 1:
+            raise ValueError("ring_attention: zig-zag balance needs an even shard length")
+        return _ring_attention_native(q, k, v, group, causal, balance, scale, return_lse)
     attend = attend or _default_attend
     merge = merge or _default_merge
     P = dist.get_world_size(group) if dist.is_initialized() else 1

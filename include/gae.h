@@ -200,6 +200,57 @@ typedef struct {
 GAE_API gae_status gae_attn_fwd(const gae_attn_args *args, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Sequence-parallel ring attention over P GPUs (no reference counterpart:
+ * the reference has no multi-GPU path; this is its long-sequence caller).
+ * One process or thread per GPU; each rank holds a contiguous shard
+ * [B, H, S, D] of one sequence of N = P*S tokens (rank r owns positions
+ * [r*S, (r+1)*S)) and receives the exact attention output of its queries
+ * against the whole sequence, with the natural-log LSE if requested.
+ *
+ * Transport: an NCCL communicator (libnccl.so.2 is loaded at run time).
+ * K/V blocks travel rank r -> r+1 by ncclSend/ncclRecv on an internal
+ * stream, overlapped with the attention kernels on the caller's stream;
+ * partial results are merged by log-sum-exp (gae_lse_merge's algebra) in
+ * fp32.  With GAE_RING_ZIGZAG and causal != 0 the shards are re-dealt so that
+ * rank r computes on chunks r and 2P-1-r of 2P (equal work per rank and
+ * step) and the output is dealt back.  Remote blocks land in this GPU's
+ * memory before any kernel reads them.
+ *
+ * The context owns a device arena (grown on demand; about 10x the shard's
+ * bytes) and a non-blocking communicator.  Waits on the communicator and,
+ * when timeout_s > 0, the completion of each gae_ring_attn_fwd are bounded
+ * by timeout_s: on expiry the communicator is aborted, the call returns
+ * GAE_ERR_TIMEOUT (GAE_ERR_COMM for an NCCL error) and the context refuses
+ * further work.  With timeout_s <= 0 the call returns once everything is
+ * enqueued (asynchronous, unbounded).  A context is used by one host thread
+ * at a time, on the device current at its creation.
+ * ---------------------------------------------------------------------- */
+#define GAE_RING_UNIQUE_ID_BYTES 128
+enum { GAE_RING_ZIGZAG = 0, GAE_RING_CONTIGUOUS = 1 };
+typedef struct gae_ring_ctx gae_ring_ctx;
+
+/* A fresh NCCL unique id (GAE_RING_UNIQUE_ID_BYTES bytes) that one rank
+ * creates and every rank passes to gae_ring_ctx_create. */
+GAE_API gae_status gae_ring_unique_id(void *unique_id);
+
+/* Joins the P-rank communicator of unique_id as `rank` (collective: every
+ * rank calls it). */
+GAE_API gae_status gae_ring_ctx_create(const void *unique_id, int rank, int world, double timeout_s,
+                                       gae_ring_ctx **ctx);
+
+/* Uses a caller-owned ncclComm_t (passed as void*; not destroyed by
+ * gae_ring_ctx_destroy). */
+GAE_API gae_status gae_ring_ctx_create_from_comm(void *nccl_comm, double timeout_s, gae_ring_ctx **ctx);
+
+/* args: this rank's shards as for gae_attn_fwd (bf16 or f16, head_dim 64 or
+ * 128, seq_q == seq_kv = S, offsets 0); balance GAE_RING_ZIGZAG (causal; S
+ * even) or GAE_RING_CONTIGUOUS.  Collective: every rank calls it with the
+ * same shapes.  With one rank it is one gae_attn_fwd launch. */
+GAE_API gae_status gae_ring_attn_fwd(gae_ring_ctx *ctx, const gae_attn_args *args, int balance, void *stream);
+
+GAE_API gae_status gae_ring_ctx_destroy(gae_ring_ctx *ctx);
+
+/* ------------------------------------------------------------------------
  * Attention backward: dQ, dK, dV of the exact attention computed by
  * gae_attn_fwd, from Q, K, V, the forward output O, the output gradient dO
  * and the forward's LSE (natural log, [batch*heads, seq_q] as gae_attn_fwd

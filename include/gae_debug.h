@@ -39,6 +39,16 @@ GAE_API gae_status gae_debug_attn_trace(void *buf, int cta);
 GAE_API gae_status gae_debug_attn_int8_logits(const gae_attn_int8_args *args, int32_t *logits,
                                               void *stream);
 
+/* The attention launches gae_ring_attn_fwd issues at ring step `step` on
+ * `rank` of `world` (shard length shard_len, zigzag != 0 for the balanced
+ * causal layout): *n_ops (at most 2) records of 7 int64 in ops: query row 0,
+ * query rows, key row 0, key rows (rows of the rank's internal zig-zag or
+ * contiguous buffer and of the step's K/V block), causal, absolute position
+ * of the first query, of the first key.  Host-only; for tests of the ring's
+ * plan without GPUs. */
+GAE_API gae_status gae_debug_ring_plan(int rank, int world, int step, int causal, int zigzag,
+                                       int64_t shard_len, int64_t *ops, int *n_ops);
+
 /* Exercises the library's bounded device-side wait: launches one thread that
  * waits on an mbarrier nothing will complete, with a limit of timeout_ns
  * (at most 1 s).  The wait gives up, records site 0x901 and the kernel exits

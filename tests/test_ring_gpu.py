@@ -1,8 +1,10 @@
-"""Ring attention on the CUDA path: every block pair through gae_attn_fwd, every
-merge through gae_lse_merge.  One GPU runs the P=1 ring in-process (zig-zag
-split into two chunks: three block pairs and one merge); with two or more
-GPUs visible, NCCL ranks (one process per GPU) run the real ring.
-Tolerance: bf16 output within 2e-2 max-abs of the fp32 oracle."""
+"""Ring attention on the CUDA path, through the C ABI (gae_ring_attn_fwd:
+re-deal, K/V rotation over NCCL, attention launches and log-sum-exp merges
+inside libgae.so).  One GPU runs the P=1 ring in-process (one launch over the
+whole sequence); with two or more GPUs visible, NCCL ranks (one process per
+GPU) run the real ring in every layout.  The backward ring is the Python
+driver over torch.distributed.
+Tolerance: bf16 output within 2e-2 max-abs of the fp32 oracle, LSE 1e-3."""
 import math
 import os
 import socket
@@ -82,9 +84,21 @@ def _nccl_worker(rank, world, port, out_dir):
     grads = ring.ring_attention_backward(qs, ks, vs, o, dos, lse, causal=True)
     torch.cuda.synchronize()
     np.save(os.path.join(out_dir, f"o{rank}.npy"), o.float().cpu().numpy())
+    np.save(os.path.join(out_dir, f"lse{rank}.npy"), lse.cpu().numpy())
     for name, t in zip(("dq", "dk", "dv"), grads):
         np.save(os.path.join(out_dir, f"{name}{rank}.npy"), t.float().cpu().numpy())
+    # the other layouts, batch 2 and head_dim 64 with a strided [B, S, H, D] view
+    for tag, causal, balance, (B2, H2, D2) in (("cc", True, "contiguous", (2, 3, 128)),
+                                               ("nc", False, "contiguous", (2, 3, 64)),
+                                               ("zz64", True, "zigzag", (2, 2, 64))):
+        q2, k2, v2 = _inputs(B2, H2, N, D2, seed=21)
+        views = [t[:, :, sl].transpose(1, 2).contiguous().cuda().transpose(1, 2) for t in (q2, k2, v2)]
+        o2, l2 = ring.ring_attention(*views, causal=causal, balance=balance, return_lse=True)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"o_{tag}{rank}.npy"), o2.float().cpu().numpy())
+        np.save(os.path.join(out_dir, f"lse_{tag}{rank}.npy"), l2.cpu().numpy())
     dist.barrier()
+    ring.release_contexts()
     dist.destroy_process_group()
 
 
@@ -97,10 +111,21 @@ def test_ring_multi_gpu(ora, tmp_path):
     mp.spawn(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     B, H, N, D = 1, 4, 512 * world, 128
     q, k, v = _inputs(B, H, N, D)
-    ref = ora.attention_batched(q.float().numpy(), k.float().numpy(), v.float().numpy(),
-                                1 / math.sqrt(D), True)
+    ref, rlse = ora.attention_batched(q.float().numpy(), k.float().numpy(), v.float().numpy(),
+                                      1 / math.sqrt(D), True, want_lse=True)
     got = np.concatenate([np.load(tmp_path / f"o{r}.npy") for r in range(world)], axis=2)
     assert float(np.abs(got - ref).max()) <= 2e-2
+    gl = np.concatenate([np.load(tmp_path / f"lse{r}.npy") for r in range(world)], axis=2)
+    assert float(np.abs(gl - rlse).max()) <= 1e-3
+    for tag, causal, (B2, H2, D2) in (("cc", True, (2, 3, 128)), ("nc", False, (2, 3, 64)),
+                                      ("zz64", True, (2, 2, 64))):
+        q2, k2, v2 = _inputs(B2, H2, N, D2, seed=21)
+        r2, rl2 = ora.attention_batched(q2.float().numpy(), k2.float().numpy(), v2.float().numpy(),
+                                        1 / math.sqrt(D2), causal, want_lse=True)
+        g2 = np.concatenate([np.load(tmp_path / f"o_{tag}{r}.npy") for r in range(world)], axis=2)
+        l2 = np.concatenate([np.load(tmp_path / f"lse_{tag}{r}.npy") for r in range(world)], axis=2)
+        assert float(np.abs(g2 - r2).max()) <= 2e-2, tag
+        assert float(np.abs(l2 - rl2).max()) <= 1e-3, tag
     do = _inputs(B, H, N, D, seed=9)[0]
     f = lambda t: t.float().numpy().reshape(B * H, N, D)
     refs = ora.attention_bwd(f(q), f(k), f(v), f(do), 1 / math.sqrt(D), True)
