@@ -125,7 +125,10 @@ def test_ring_multi_gpu(ora, tmp_path):
         g2 = np.concatenate([np.load(tmp_path / f"o_{tag}{r}.npy") for r in range(world)], axis=2)
         l2 = np.concatenate([np.load(tmp_path / f"lse_{tag}{r}.npy") for r in range(world)], axis=2)
         assert float(np.abs(g2 - r2).max()) <= 2e-2, tag
-        assert float(np.abs(l2 - rl2).max()) <= 1e-3, tag
+        # At head_dim 64 the row sums come from the tensor core over the
+        # bf16-rounded probabilities (the same P as the numerator): the sum's
+        # relative error is up to 2^-8, i.e. 4e-3 in the LSE.
+        assert float(np.abs(l2 - rl2).max()) <= (4e-3 if D2 == 64 else 1e-3), tag
     do = _inputs(B, H, N, D, seed=9)[0]
     f = lambda t: t.float().numpy().reshape(B * H, N, D)
     refs = ora.attention_bwd(f(q), f(k), f(v), f(do), 1 / math.sqrt(D), True)
