@@ -89,6 +89,24 @@ def ref_symphony128():
     return L
 
 
+REF_KERNEL_BENCH_PATH = os.path.join(_HERE, "_ref", "libref_kernel_bench.so")
+
+
+def ref_kernel_bench():
+    """ctypes handle on the reference's published attention chain
+    (cuda_src/waller_kernel_bench.cu: cuBLAS score/PV tiles + SIMT softmax)
+    built from its source (oracle/ref_kernel_bench.cu), or None where it was
+    not built.  ref_kernel_bench_tflops(seq_len, head_dim, tile, iters) runs
+    the reference's own run_benchmark on one fp16 sequence and returns its
+    TFLOPS figure (4 N^2 d per iteration)."""
+    if not os.path.exists(REF_KERNEL_BENCH_PATH):
+        return None
+    L = C.CDLL(REF_KERNEL_BENCH_PATH)
+    L.ref_kernel_bench_tflops.restype = C.c_float
+    L.ref_kernel_bench_tflops.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+    return L
+
+
 def ref_symphony():
     """ctypes handle on the reference's own symphony kernel built from its
     source (oracle/ref_symphony.cu), or None where it was not built.  Takes
