@@ -795,6 +795,13 @@ def main():
     }
     if north_star is not None:
         line["north_star_131072"] = north_star
+    if is_int8:
+        # Survey 8(d)'s split: QK^T (half the ops) against the int8 tensor peak,
+        # taken as twice the measured bf16 peak (the dense int8 rate is twice
+        # bf16's), and P*V against the bf16 peak.
+        t_s = ms_step * 1e-3
+        line["pct_of_peak_split"] = 100.0 * (flops / 2 / (2 * peak * 1e12) + flops / 2 / (peak * 1e12)) / t_s
+        line["pct_of_peak_split_note"] = "QK^T ops / (2 x measured bf16 peak) + PV FLOP / bf16 peak, over the step time"
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
