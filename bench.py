@@ -75,6 +75,10 @@ WORKLOADS = {
     # benchmark's largest single-launch length with HEAD_DIM 64 (:17, :407)
     "symphony": dict(B=1, H=1, N=131072, D=64, causal=True, cfg="symphony-layer-131072-d64",
                      sym=True, metric="fused symphony layer TFLOPS (d=64, int8 K/V)"),
+    # the reference's head_dim-256 fused layer (waller_fused_realistic.cu:151-274)
+    # at its benchmark's largest length (:490)
+    "symphony256": dict(B=1, H=1, N=65536, D=256, causal=True, cfg="symphony-layer-65536-d256",
+                        sym=True, metric="fused symphony layer TFLOPS (d=256, int8 K/V)"),
 }
 METRIC = "fused-attention TFLOPS (bf16 d=128)"
 
@@ -345,19 +349,24 @@ def run_reference_kernel(args, w):
     distribution; CUDA-event timed.  A comparison point, not the CPU arm."""
     import torch
     from oracle import oracle
-    L = oracle.ref_symphony()
-    if L is None:
+    N, D = w["N"], w["D"]
+    if D == 64:
+        L = oracle.ref_symphony()
+        fwd = L.ref_symphony_fwd if L is not None else None
+    else:
+        L = oracle.ref_symphony128()
+        fwd = getattr(L, f"ref_symphony{D}_fwd", None) if L is not None else None
+    if fwd is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference symphony kernel not built (oracle/_ref missing)"}))
         return 0
-    N, D = w["N"], w["D"]
     a = {n_: torch.from_numpy(v_).cuda() for n_, v_ in symphony_arrays(N, D, 1000).items()}
     out = torch.empty_like(a["x"])
     tf = np.asarray((1.0 / (math.sqrt(D) * 127.0 * 127.0), 1.0, 1.0, 1.0, 1e-6, 1.0, 1.0), np.float32)
     st = torch.cuda.current_stream()
 
     def launch():
-        rc = L.ref_symphony_fwd(a["k"].data_ptr(), a["v"].data_ptr(), a["w_up"].data_ptr(),
+        rc = fwd(a["k"].data_ptr(), a["v"].data_ptr(), a["w_up"].data_ptr(),
                                 a["w_down"].data_ptr(), a["n1"].data_ptr(), a["n2"].data_ptr(),
                                 a["x"].data_ptr(), out.data_ptr(), N, tf, 0, st.cuda_stream)
         if rc != 0:

@@ -697,15 +697,15 @@ gae_status check_layer(const gae_layer_args *a, const gae_layer_weights *w) {
         if (!q) return fail(GAE_ERR_INVALID_ARG, "NULL layer weight");
     return GAE_OK;
 }
-template <int D>
-gae_status launch_symphony_post(const float *x, const __half *attn, const float *w_up,
+template <int D, typename TA>
+gae_status launch_symphony_post(const float *x, const TA *attn, const float *w_up,
                                       const float *w_down, const float *n1, const float *n2, int64_t n,
                                       const gae::SymTuning &t, float *out, cudaStream_t st) {
     using P = gae::SymPost<D>;
-    gae_status s = set_smem(gae::symphony_post_kernel<D>, (int)P::kSmem);
+    gae_status s = set_smem(gae::symphony_post_kernel<D, TA>, (int)P::kSmem);
     if (s != GAE_OK) return s;
     const unsigned blocks = (unsigned)((n + P::T - 1) / P::T);
-    gae::symphony_post_kernel<D><<<blocks, P::kThreads, P::kSmem, st>>>(x, attn, w_up, w_down, n1, n2, n, t, out);
+    gae::symphony_post_kernel<D, TA><<<blocks, P::kThreads, P::kSmem, st>>>(x, attn, w_up, w_down, n1, n2, n, t, out);
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }
@@ -964,8 +964,9 @@ gae_status gae_attn_bwd(const gae_attn_bwd_args *args, void *stream) {
 
 size_t gae_symphony_workspace_bytes(int64_t seq_len, int64_t head_dim) {
     if (seq_len < 1 || head_dim < 1) return 0;
-    const size_t region = ((size_t)seq_len * head_dim * 2 + 255) & ~(size_t)255;
-    return 4 * region;  // q, k, v (f16) and the attention output (f16)
+    const size_t esize = head_dim == 256 ? 4 : 2;  // fp32 operands at 256, f16 below
+    const size_t region = ((size_t)seq_len * head_dim * esize + 255) & ~(size_t)255;
+    return 4 * region;  // q, k, v and the attention output
 }
 
 gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v, const float *w_up,
@@ -975,7 +976,8 @@ gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v
     if (n == 0) return GAE_OK;
     if (!input || !k || !v || !w_up || !w_down || !norm1_w || !norm2_w || !tf || !output || !workspace)
         return fail(GAE_ERR_INVALID_ARG, "NULL pointer in symphony arguments");
-    if (n < 0 || (d != 64 && d != 128)) return fail(GAE_ERR_UNSUPPORTED, "symphony supports head_dim 64 or 128");
+    if (n < 0 || (d != 64 && d != 128 && d != 256))
+        return fail(GAE_ERR_UNSUPPORTED, "symphony supports head_dim 64, 128 or 256");
     if (!(tf->attn_temperature != 0.f)) return fail(GAE_ERR_INVALID_ARG, "attn_temperature is zero");
     const size_t need = gae_symphony_workspace_bytes(n, d);
     if (workspace_bytes < need) return fail(GAE_ERR_INVALID_ARG, "workspace too small: %zu < %zu", workspace_bytes, need);
@@ -984,30 +986,43 @@ gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const size_t region = need / 4;
     char *ws = static_cast<char *>(workspace);
-    __half *qh = (__half *)ws, *kh = (__half *)(ws + region), *vh = (__half *)(ws + 2 * region),
-           *oh = (__half *)(ws + 3 * region);
     const int64_t elems = n * d;
-    gae::symphony_prep_kernel<<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(input, k, v, qh, kh, vh, elems);
-    GAE_CUDA_TRY(cudaGetLastError());
     gae_attn_args a;
     memset(&a, 0, sizeof(a));
-    a.q = qh; a.k = kh; a.v = vh; a.o = oh;
+    a.q = ws; a.k = ws + region; a.v = ws + 2 * region; a.o = ws + 3 * region;
     a.batch = 1; a.heads = 1; a.seq_q = n; a.seq_kv = n; a.head_dim = d;
     const int64_t str[3] = {n * d, n * d, d};
     memcpy(a.q_stride, str, sizeof str); memcpy(a.k_stride, str, sizeof str);
     memcpy(a.v_stride, str, sizeof str); memcpy(a.o_stride, str, sizeof str);
-    a.dtype = GAE_DTYPE_F16;
     a.causal = 1;
     a.scale = tf->attn_scale / tf->attn_temperature;
     if (!(a.scale >= 0.f)) return fail(GAE_ERR_UNSUPPORTED, "attn_scale / attn_temperature must be >= 0");
-    gae_status s = launch_attn_tc(&a, st);
-    if (s != GAE_OK) return s;
+    gae_status s;
+    if (d == 256) {
+        // head_dim 256: the tensor-core kernel's TMEM holds two 128-row Q tiles'
+        // S and O only up to head_dim 128, so the attention runs on the
+        // CUDA-core fp32 kernel (exact integer dot products, |dot| < 2^24).
+        gae::symphony_prep_kernel<float><<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(
+            input, k, v, (float *)a.q, (float *)a.k, (float *)a.v, elems);
+        GAE_CUDA_TRY(cudaGetLastError());
+        a.dtype = GAE_DTYPE_F32;
+        if ((s = launch_attn_f32(&a, st)) != GAE_OK) return s;
+    } else {
+        gae::symphony_prep_kernel<__half><<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(
+            input, k, v, (__half *)a.q, (__half *)a.k, (__half *)a.v, elems);
+        GAE_CUDA_TRY(cudaGetLastError());
+        a.dtype = GAE_DTYPE_F16;
+        if ((s = launch_attn_tc(&a, st)) != GAE_OK) return s;
+    }
     gae::SymTuning t;
     t.attn_scale = tf->attn_scale; t.attn_temperature = tf->attn_temperature;
     t.residual_alpha = tf->residual_alpha; t.residual_beta = tf->residual_beta; t.norm_eps = tf->norm_eps;
     t.activation_type = tf->activation_type; t.mlp_gate = tf->mlp_gate; t.output_scale = tf->output_scale;
+    const __half *oh = static_cast<const __half *>(a.o);
     if (d == 64) s = launch_symphony_post<64>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
-    else s = launch_symphony_post<128>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
+    else if (d == 128) s = launch_symphony_post<128>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
+    else s = launch_symphony_post<256>(input, static_cast<const float *>(a.o), w_up, w_down, norm1_w, norm2_w, n,
+                                       t, output, st);
     if (s != GAE_OK) return s;
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;

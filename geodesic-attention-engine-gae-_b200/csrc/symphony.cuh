@@ -25,15 +25,24 @@ struct SymTuning {
     float mlp_gate, output_scale;
 };
 
-__global__ void symphony_prep_kernel(const float *x, const int8_t *k, const int8_t *v, __half *qh,
-                                     __half *kh, __half *vh, int64_t n_elems) {
+// TO: __half for the tensor-core attention (head_dim 64/128), float for the
+// CUDA-core one (head_dim 256); both hold the int8 values exactly.
+template <typename TO>
+__global__ void symphony_prep_kernel(const float *x, const int8_t *k, const int8_t *v, TO *qh, TO *kh, TO *vh,
+                                     int64_t n_elems) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_elems) return;
     // (int8_t) of a float truncates toward zero, as the reference's cast does.
     const int q = (int)fmaxf(-127.0f, fminf(127.0f, x[i] * 127.0f));
-    qh[i] = __int2half_rn(q);
-    kh[i] = __int2half_rn((int)k[i]);
-    vh[i] = __int2half_rn((int)v[i]);
+    if constexpr (sizeof(TO) == 2) {
+        qh[i] = __int2half_rn(q);
+        kh[i] = __int2half_rn((int)k[i]);
+        vh[i] = __int2half_rn((int)v[i]);
+    } else {
+        qh[i] = (float)q;
+        kh[i] = (float)k[i];
+        vh[i] = (float)v[i];
+    }
 }
 
 // waller_fused_layer.cu:35-46; any other type is the identity (its default branch).
@@ -46,8 +55,9 @@ __device__ __forceinline__ float sym_activation(float x, int type) {
     }
 }
 
-// Post kernel tiling: T tokens per CTA (64 at head_dim 64, 32 at 128), 256
-// threads, 8 warps.  Both projections are register-tiled outer products over
+// Post kernel tiling: T tokens per CTA (64 at head_dim 64, 32 at 128 and 256),
+// 256 threads, 8 warps (each warp walks as many column strips as the width
+// needs: one at 64 and 128, two at 256).  Both projections are register-tiled outer products over
 // transposed shared-memory operands, so that a warp's loads per k-step are a
 // few 128-byte wavefronts for 16-64 FMA instructions:
 //   up   [T, D] x [D, 4D]: warp tile 32 tokens x 64 columns, lane tile 8 x 8
@@ -57,17 +67,18 @@ __device__ __forceinline__ float sym_activation(float x, int type) {
 template <int D> struct SymPost {
     static constexpr int M = 4 * D;
     static constexpr int T = D == 64 ? 64 : 32;
+    static_assert(D == 64 || D == 128 || D == 256, "head_dim 64, 128 or 256");
     static constexpr int kThreads = 256;
     static constexpr int kTP = T + 4;  // pitch (floats) of the token-minor buffers
     static constexpr int kUpWarpsT = T / 32, kUpWarpsC = 8 / kUpWarpsT;  // 64-column strips
     static constexpr int kDnWarpsT = T / 16, kDnWarpsC = 8 / kDnWarpsT;  // 32-column strips
-    static_assert(kUpWarpsC * 64 == M, "up tiling");
-    static_assert(kDnWarpsC * 32 == D, "down tiling");
+    static_assert(M % (kUpWarpsC * 64) == 0, "up tiling");
+    static_assert(D % (kDnWarpsC * 32) == 0, "down tiling");
     static constexpr size_t kSmem = sizeof(float) * ((size_t)T * D + (size_t)D * kTP + (size_t)M * kTP);
 };
 
-template <int D>
-__global__ void __launch_bounds__(256, 2) symphony_post_kernel(const float *x, const __half *attn,
+template <int D, typename TA>
+__global__ void __launch_bounds__(256, D == 256 ? 1 : 2) symphony_post_kernel(const float *x, const TA *attn,
                                                                const float *w_up, const float *w_down,
                                                                const float *n1, const float *n2, int64_t n,
                                                                SymTuning tf, float *out) {
@@ -87,9 +98,16 @@ __global__ void __launch_bounds__(256, 2) symphony_post_kernel(const float *x, c
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (row0 + i / D < n) {
             const float4 xv = __ldg(reinterpret_cast<const float4 *>(x + row0 * D + i));
-            const uint2 ah = *reinterpret_cast<const uint2 *>(attn + row0 * D + i);
-            const float2 a01 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.x));
-            const float2 a23 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.y));
+            float2 a01, a23;
+            if constexpr (sizeof(TA) == 2) {
+                const uint2 ah = *reinterpret_cast<const uint2 *>(attn + row0 * D + i);
+                a01 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.x));
+                a23 = __half22float2(*reinterpret_cast<const __half2 *>(&ah.y));
+            } else {
+                const float4 af = *reinterpret_cast<const float4 *>(attn + row0 * D + i);
+                a01 = make_float2(af.x, af.y);
+                a23 = make_float2(af.z, af.w);
+            }
             v = make_float4(xv.x * tf.residual_alpha + a01.x, xv.y * tf.residual_alpha + a01.y,
                             xv.z * tf.residual_alpha + a23.x, xv.w * tf.residual_alpha + a23.y);
         }
@@ -118,9 +136,9 @@ __global__ void __launch_bounds__(256, 2) symphony_post_kernel(const float *x, c
     __syncthreads();
 
     // Up projection + activation (reference :207-218).
-    {
+    for (int strip = warp / P::kUpWarpsT; strip < M / 64; strip += P::kUpWarpsC) {
         const int t0 = (warp % P::kUpWarpsT) * 32 + (lane >> 3) * 8;
-        const int j0 = (warp / P::kUpWarpsT) * 64 + (lane & 7) * 8;
+        const int j0 = strip * 64 + (lane & 7) * 8;
         float acc[8][8];
 #pragma unroll
         for (int a = 0; a < 8; ++a)
@@ -158,9 +176,9 @@ __global__ void __launch_bounds__(256, 2) symphony_post_kernel(const float *x, c
     __syncthreads();
 
     // Down projection * gate, then residual 2 in place (reference :220-238).
-    {
+    for (int strip = warp / P::kDnWarpsT; strip < D / 32; strip += P::kDnWarpsC) {
         const int t0 = (warp % P::kDnWarpsT) * 16 + (lane >> 3) * 4;
-        const int c0 = (warp / P::kDnWarpsT) * 32 + (lane & 7) * 4;
+        const int c0 = strip * 32 + (lane & 7) * 4;
         float acc[4][4];
 #pragma unroll
         for (int a = 0; a < 4; ++a)

@@ -430,7 +430,9 @@ GAE_API gae_status gae_linear_fwd(const void *x, const void *w, const float *bia
  * reference's `default:` branch, @ w_down [4d, d], * mlp_gate) ->
  * state*residual_beta + mlp -> RMSNorm(norm2_w) -> * output_scale.
  * input/output fp32 [seq_len, head_dim], k/v int8 [seq_len, head_dim], weights
- * fp32 row-major; head_dim 64 or 128; input, output, w_up, w_down and the
+ * fp32 row-major; head_dim 64 or 128 (tensor-core attention) or 256 (the
+ * reference's waller_fused_256, cuda_src/waller_fused_realistic.cu:151-274;
+ * attention on the CUDA cores in fp32); input, output, w_up, w_down and the
  * workspace 16-byte aligned.  `workspace`: device memory of at least
  * gae_symphony_workspace_bytes(seq_len, head_dim) bytes.
  * ---------------------------------------------------------------------- */

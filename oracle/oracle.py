@@ -86,6 +86,8 @@ def ref_symphony128():
     L = C.CDLL(REF_SYMPHONY128_PATH)
     vp = C.c_void_p
     L.ref_symphony128_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, C.c_int, _f32p, C.c_int, vp]
+    if hasattr(L, "ref_symphony256_fwd"):  # head_dim 256 (waller_fused_256)
+        L.ref_symphony256_fwd.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, C.c_int, _f32p, C.c_int, vp]
     return L
 
 

@@ -33,5 +33,6 @@ def test_flop_counts_and_profiles():
     assert bench.symphony_flops(4, 8) == bench.attn_flops(1, 1, 4, 4, 8, True) + 16 * 4 * 64 + 8 * 32
     # the default workload's DRAM traffic comes from the committed ncu summary
     assert bench.profile_traffic("mha") is not None and bench.profile_traffic("mha") > 4e8
+    assert bench.profile_traffic("ring") is not None and bench.profile_traffic("ring") > 8e9  # the default
     for name, w in bench.WORKLOADS.items():
-        assert w["cfg"] and w["D"] in (64, 128), name
+        assert w["cfg"] and w["D"] in (64, 128, 256), name

@@ -38,7 +38,7 @@ def _ora_tuning(tf):
             tf.mlp_gate, tf.output_scale)
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 @pytest.mark.parametrize("act", [0, 1, 2, 3])
 def test_symphony_matches_oracle(gae, ora, d, act):
     n = 1000
@@ -77,11 +77,12 @@ def test_symphony_rejects_bad_args(gae):
                              workspace=small)
 
 
-@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("d", [64, 128, 256])
 def test_reference_kernel_pins_oracle_and_product(gae, ora, d):
     """The reference's own fused-layer kernels, built from its source into
     oracle/_ref (d=64: waller_fused_symphony_kernel, waller_fused_layer.cu;
-    d=128: waller_fused_128, waller_fused_realistic.cu:26-148), on the
+    d=128 / 256: waller_fused_128 / waller_fused_256,
+    waller_fused_realistic.cu:26-148 / :151-274), on the
     reference benchmark's input distribution (uniform inputs, small uniform
     weights, unit norms) against the oracle and against gae_symphony_fwd.
 
@@ -96,7 +97,8 @@ def test_reference_kernel_pins_oracle_and_product(gae, ora, d):
         launch = ref_lib.ref_symphony_fwd if ref_lib is not None else None
     else:
         ref_lib = ora.ref_symphony128()
-        launch = ref_lib.ref_symphony128_fwd if ref_lib is not None else None
+        name = "ref_symphony128_fwd" if d == 128 else "ref_symphony256_fwd"
+        launch = getattr(ref_lib, name, None) if ref_lib is not None else None
     if launch is None:
         pytest.skip("reference fused-layer kernel not built (no reference tree where build() ran)")
     n = 2048
