@@ -100,23 +100,30 @@ enum AttnWaitSite : unsigned {
     kSiteDone = 0x107,
 };
 
-enum AttnMode : int { kModeBF16 = 0, kModeF16 = 1, kModeInt8 = 2 };
+// kModeSymI8: the symphony layer's integer attention at head_dim 256 --
+// Q and K int8 rows of 2*D values (QK^T over 256 dimensions on the int8
+// tensor cores, exact int32), V, P and O f16 over D = 128 columns (one half
+// of the 256-wide V per launch), no per-row query scale (q_scale NULL).
+enum AttnMode : int { kModeBF16 = 0, kModeF16 = 1, kModeInt8 = 2, kModeSymI8 = 3 };
 
 template <int D, int kMode>
 struct AttnCfg {
-    static constexpr bool kInt8 = kMode == kModeInt8;
+    static constexpr bool kInt8 = kMode == kModeInt8 || kMode == kModeSymI8;
     static constexpr int kBlockM = 128;                      // rows per Q tile
     static constexpr int kBlockN = 128;                      // keys per K/V tile
     static constexpr int kBoxBytes = 128 * 128;              // 128 rows x 128 B
-    static constexpr int kQKRowBytes = D * (kInt8 ? 1 : 2);  // Q/K row
+    static constexpr int kQKRowBytes = (kMode == kModeInt8) ? D : 2 * D;  // Q/K row
     static constexpr int kQKBoxes = kQKRowBytes / 128;       // 128-byte swizzle boxes per Q/K row
     static constexpr int kVBoxes = D * 2 / 128;              // V is 16-bit in every mode
     static constexpr int kQTileBytes = kQKBoxes * kBoxBytes;
     static constexpr int kKTileBytes = kQKBoxes * kBoxBytes;
     static constexpr int kVTileBytes = kVBoxes * kBoxBytes;
     static constexpr int kKScaleBytes = kInt8 ? kBlockN * 4 : 0;  // per-key scales after K
-    static constexpr int kSlotBytes = kVTileBytes;               // >= K tile + its scales
-    static constexpr int kStages = (D == 128) ? (kInt8 ? 5 : 4) : 8;  // K/V ring slots
+    // A slot holds a V tile or a K tile with its scales (1024-byte multiple).
+    static constexpr int kSlotBytes = (kKTileBytes + kKScaleBytes > kVTileBytes)
+                                          ? (kKTileBytes + kKScaleBytes + 1023) / 1024 * 1024
+                                          : kVTileBytes;
+    static constexpr int kStages = (D == 128) ? (kMode == kModeInt8 ? 5 : 4) : 8;  // K/V ring slots
     static constexpr int kQBytes = 2 * kQTileBytes;  // one unit's two Q tiles
     // Q buffers: at head_dim 64 (persistent grid, short units) the next unit's
     // Q loads while the current one runs; at 128 shared memory allows one.
@@ -169,7 +176,7 @@ struct AttnCfg {
 #endif
 template <int D, int kMode>
 __device__ __forceinline__ constexpr bool use_poly_exp(int e) {
-    constexpr int kPeriod = (kMode == kModeInt8) ? GAE_EMU_PERIOD_INT8
+    constexpr int kPeriod = (kMode == kModeInt8 || kMode == kModeSymI8) ? GAE_EMU_PERIOD_INT8
                             : (D == 64)          ? GAE_EMU_PERIOD_D64
                                                  : GAE_EMU_PERIOD_D128;
     return kPeriod > 0 && (e % (kPeriod > 0 ? kPeriod : 1)) == kPeriod - 1;
@@ -181,7 +188,7 @@ __device__ __forceinline__ constexpr bool use_poly_exp(int e) {
 template <int D, int kMode, bool kDump = false>
 __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_constant__ AttnParams p) {
     using Cfg = AttnCfg<D, kMode>;
-    constexpr bool kBF16 = kMode != kModeF16;  // P and O are bf16 in bf16 and int8 modes
+    constexpr bool kBF16 = kMode == kModeBF16 || kMode == kModeInt8;  // P and O bf16 (else f16)
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the 128B-swizzle atoms.
     const uint32_t raw_addr = smem_u32(smem_raw);
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         // the query row's dequantisation scale in int8 mode.
         float sl2 = p.scale_log2;
         if constexpr (Cfg::kInt8)
-            sl2 *= (q_local < p.Nq) ? p.q_scale[(int64_t)bh * p.Nq + q_local] : 0.f;
+            sl2 *= (q_local < p.Nq) ? (p.q_scale ? p.q_scale[(int64_t)bh * p.Nq + q_local] : 1.f) : 0.f;
         // A zero factor (zero scale, or an all-zero int8 query row) makes every
         // visible score equal; a tiny positive factor keeps that result while
         // masked (-inf) entries still map to probability 0 instead of NaN.

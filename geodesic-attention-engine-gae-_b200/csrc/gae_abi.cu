@@ -359,6 +359,32 @@ gae_status launch_attn_int8(const gae_attn_int8_args *a, cudaStream_t st, int32_
     return launch_tc<128, gae::kModeInt8>(p, grid, st);
 }
 
+// The symphony layer's integer attention at head_dim 256 (kModeSymI8): q, k
+// int8 [n, 256]; v f16 [n, 256] of which columns [half*128, half*128+128) are
+// attended; o f16 [n, 256], the same columns written; ones: fp32 [n4] of 1.0
+// (the per-key scale row), n4 = n rounded up to 4.  Causal.
+gae_status launch_attn_sym_i8(const int8_t *q, const int8_t *k, const __half *v, __half *o, const float *ones,
+                              int64_t n, int64_t n4, float scale, int half, cudaStream_t st) {
+    gae::AttnParams p;
+    memset(&p, 0, sizeof(p));
+    gae_status s;
+    if ((s = make_map_4d(&p.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 1, 1, n, 256, n * 256, n * 256, 256, 128)) != GAE_OK) return s;
+    if ((s = make_map_4d(&p.tm_k, k, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 1, 1, n, 256, n * 256, n * 256, 256, 128)) != GAE_OK) return s;
+    if ((s = make_map_4d(&p.tm_v, v + half * 128, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 1, 1, n, 128, n * 256, n * 256,
+                         256, 128)) != GAE_OK)
+        return s;
+    if ((s = make_map_2d_f32(&p.tm_ks, ones, n4, 1)) != GAE_OK) return s;
+    p.q_scale = nullptr;
+    p.o = o + half * 128;
+    p.o_sb = n * 256; p.o_sh = n * 256; p.o_ss = 256;
+    p.B = 1; p.H = 1; p.Nq = (int)n; p.Nkv = (int)n;
+    p.n_qpairs = (int)((n + 255) / 256);
+    p.causal = 1;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.head_major = 1;
+    return launch_tc<128, gae::kModeSymI8>(p, dim3((unsigned)p.n_qpairs), st);
+}
+
 gae_status launch_int8_logits(const int8_t *q, const int8_t *k, int64_t BH, int64_t Nq, int64_t Nkv,
                               int64_t D, int32_t *out, cudaStream_t st) {
     if (D != 128) return fail(GAE_ERR_UNSUPPORTED, "int8 logits support head_dim 128");
@@ -964,9 +990,10 @@ gae_status gae_attn_bwd(const gae_attn_bwd_args *args, void *stream) {
 
 size_t gae_symphony_workspace_bytes(int64_t seq_len, int64_t head_dim) {
     if (seq_len < 1 || head_dim < 1) return 0;
-    const size_t esize = head_dim == 256 ? 4 : 2;  // fp32 operands at 256, f16 below
-    const size_t region = ((size_t)seq_len * head_dim * esize + 255) & ~(size_t)255;
-    return 4 * region;  // q, k, v and the attention output
+    const size_t region = ((size_t)seq_len * head_dim * 2 + 255) & ~(size_t)255;
+    if (head_dim == 256)  // q int8, v f16, the attention output f16, a row of ones
+        return 3 * region + ((((size_t)seq_len + 3) / 4 * 16 + 255) & ~(size_t)255);
+    return 4 * region;  // q, k, v (f16) and the attention output (f16)
 }
 
 gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v, const float *w_up,
@@ -999,14 +1026,24 @@ gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v
     if (!(a.scale >= 0.f)) return fail(GAE_ERR_UNSUPPORTED, "attn_scale / attn_temperature must be >= 0");
     gae_status s;
     if (d == 256) {
-        // head_dim 256: the tensor-core kernel's TMEM holds two 128-row Q tiles'
-        // S and O only up to head_dim 128, so the attention runs on the
-        // CUDA-core fp32 kernel (exact integer dot products, |dot| < 2^24).
-        gae::symphony_prep_kernel<float><<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(
-            input, k, v, (float *)a.q, (float *)a.k, (float *)a.v, elems);
+        // head_dim 256: QK^T over the 256 int8 dimensions on the int8 tensor
+        // cores (exact int32 dots, the reference's own arithmetic), P*V in
+        // two launches over the two 128-column halves of V (TMEM holds two
+        // 128-row Q tiles' S and O up to 128 columns of O each); S is
+        // recomputed by the second launch at the int8 rate.
+        const size_t region = ((size_t)n * d * 2 + 255) & ~(size_t)255;
+        int8_t *q8 = reinterpret_cast<int8_t *>(ws);
+        __half *vh = reinterpret_cast<__half *>(ws + region);
+        __half *oh16 = reinterpret_cast<__half *>(ws + 2 * region);
+        float *ones = reinterpret_cast<float *>(ws + 3 * region);
+        const int64_t n4 = (n + 3) / 4 * 4;
+        gae::symphony_prep_i8_kernel<<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(input, v, q8, vh, ones, elems,
+                                                                                      n4);
         GAE_CUDA_TRY(cudaGetLastError());
-        a.dtype = GAE_DTYPE_F32;
-        if ((s = launch_attn_f32(&a, st)) != GAE_OK) return s;
+        if (!aligned16(k)) return fail(GAE_ERR_INVALID_ARG, "symphony: k must be 16-byte aligned at head_dim 256");
+        for (int half = 0; half < 2; ++half)
+            if ((s = launch_attn_sym_i8(q8, k, vh, oh16, ones, n, n4, a.scale, half, st)) != GAE_OK) return s;
+        a.o = oh16;
     } else {
         gae::symphony_prep_kernel<__half><<<(unsigned)((elems + 255) / 256), 256, 0, st>>>(
             input, k, v, (__half *)a.q, (__half *)a.k, (__half *)a.v, elems);
@@ -1021,8 +1058,7 @@ gae_status gae_symphony_fwd(const float *input, const int8_t *k, const int8_t *v
     const __half *oh = static_cast<const __half *>(a.o);
     if (d == 64) s = launch_symphony_post<64>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
     else if (d == 128) s = launch_symphony_post<128>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
-    else s = launch_symphony_post<256>(input, static_cast<const float *>(a.o), w_up, w_down, norm1_w, norm2_w, n,
-                                       t, output, st);
+    else s = launch_symphony_post<256>(input, oh, w_up, w_down, norm1_w, norm2_w, n, t, output, st);
     if (s != GAE_OK) return s;
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;

@@ -45,6 +45,20 @@ __global__ void symphony_prep_kernel(const float *x, const int8_t *k, const int8
     }
 }
 
+// head_dim 256 (the int8 tensor-core path): Q = trunc(clamp(x * 127)) as
+// int8 rows of 256, V widened to f16 (exact), and the per-key scale row of
+// ones that the int8 attention kernel multiplies the logits by (padded to a
+// multiple of 4 for its TMA rows).
+__global__ void symphony_prep_i8_kernel(const float *x, const int8_t *v, int8_t *q8, __half *vh, float *ones,
+                                        int64_t n_elems, int64_t n_ones) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_elems) {
+        q8[i] = (int8_t)(int)fmaxf(-127.0f, fminf(127.0f, x[i] * 127.0f));
+        vh[i] = __int2half_rn((int)v[i]);
+    }
+    if (i < n_ones) ones[i] = 1.0f;
+}
+
 // waller_fused_layer.cu:35-46; any other type is the identity (its default branch).
 __device__ __forceinline__ float sym_activation(float x, int type) {
     switch (type) {

@@ -127,10 +127,44 @@ def test_reference_kernel_pins_oracle_and_product(gae, ora, d):
         torch.cuda.synchronize()
         ref_gpu = out_ref.cpu().numpy()
         oracle_out = ora.symphony_layer(x, k, v, w_up, w_down, n1, n2, tfa, tf.activation_type)
+        rows = _reference_defined_rows(n, d)
         # oracle vs the reference kernel: same op order, fp32 throughout; only
         # expf/tanhf/rsqrtf ulps and the reference's FMA contraction differ.
-        assert float(np.abs(oracle_out - ref_gpu).max()) <= 1e-3
+        assert float(np.abs(oracle_out[rows] - ref_gpu[rows]).max()) <= 1e-3
         got = gae.symphony_forward(dev["x"], dev["k"], dev["v"], dev["w_up"], dev["w_down"],
                                    dev["n1"], dev["n2"], tf).cpu().numpy()
-        err = np.abs(got - ref_gpu) / np.maximum(1.0, np.abs(ref_gpu))
+        err = np.abs(got[rows] - ref_gpu[rows]) / np.maximum(1.0, np.abs(ref_gpu[rows]))
         assert float(err.max()) <= 2e-2
+        # everywhere: the library against the oracle
+        assert float((np.abs(got - oracle_out) / np.maximum(1.0, np.abs(oracle_out))).max()) <= 2e-2
+
+
+def _reference_defined_rows(n, d):
+    """Rows whose reference output is defined.  waller_fused_256 (d=256)
+    stages K/V in tiles of 48 keys for blocks of 32 rows, each thread with
+    its own tile length min(48, row + 1 - tile_start) and loading entries
+    tid, tid + 32 below it (waller_fused_realistic.cu:195-209).  In a block
+    whose rows are not aligned to the tiles, an entry i >= 32 of a tile is
+    loaded by thread i - 32 only if that thread's own (shorter) tile reaches
+    it, and threads that already left the loop load nothing -- so some rows
+    read K/V entries that were never written (rows 48-63, 80-95, ... of
+    every length).  Its 64- and 128-wide kernels (tiles of 128 and 96 keys,
+    multiples of the block) load every entry.  This simulates the loads and
+    keeps the rows whose every read entry was written."""
+    if d != 256:
+        return np.arange(n)
+    tile, block = 48, 32
+    ok = np.ones(n, bool)
+    for r0 in range(0, n, block):
+        rows = np.arange(r0, min(r0 + block, n))
+        for ts in range(0, int(rows[-1]) + 1, tile):
+            live = rows[ts < rows + 1]                      # threads still in the tile loop
+            tlen = np.minimum(tile, live + 1 - ts)          # each live thread's tile length
+            loaded = np.zeros(tile, bool)
+            for r, ln in zip(live, tlen):
+                i = np.arange((r - r0) % block, ln, block)
+                loaded[i] = True
+            for r, ln in zip(live, tlen):                   # a row reads entries [0, ln)
+                if not loaded[:ln].all():
+                    ok[r] = False
+    return np.nonzero(ok)[0]
