@@ -617,7 +617,11 @@ gae_status launch_layernorm(const void *x, const void *res, void *sum_out, void 
         (sum_out && !aligned16(sum_out)))
         return fail(GAE_ERR_INVALID_ARG, "layernorm operands must be 16-byte aligned");
     const int warps = 8;
-    dim3 grid((unsigned)((rows + warps - 1) / warps));
+    // Persistent warps: two CTAs of 8 warps per SM (resident at 128
+    // registers a thread), each warp walking rows.
+    const int64_t blocks_needed = (rows + warps - 1) / warps;
+    const int64_t blocks_cap = (int64_t)num_sms() * 2;
+    dim3 grid((unsigned)(blocks_needed < blocks_cap ? blocks_needed : blocks_cap));
     const int per_lane = (int)((d + 255) / 256);
 #define GAE_LN(K)                                                                                 \
     gae::layernorm_kernel<K><<<grid, warps * 32, 0, st>>>(                                        \

@@ -13,7 +13,8 @@
 //     eight epilogue warps drain the other accumulator (thread = output row,
 //     two warps per row quarter, one per column half)
 //     and fuse bias, tanh-GELU or the residual add, writing bf16.
-//   * layernorm_kernel: one warp per row, 16-byte vector loads, fp32
+//   * layernorm_kernel: one warp per row (persistent warps, gamma/beta
+//     in registers), 16-byte vector loads, fp32
 //     statistics (population variance, eps inside the square root, as
 //     layernorm.rs:6-17), optional fused residual add.
 #pragma once
@@ -444,72 +445,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
 // flight per SM (the kernel is HBM-bound).
 constexpr int kLnMaxChunks = 16;  // 16 x 8 x 32 = 4096 elements per row at most
 
+// Persistent rows: each warp walks rows warp_id, warp_id + total_warps, ...
+// with gamma and beta held in registers for all of them (loaded once), and
+// the next row's 16-byte chunks loaded before the current row is reduced.
 template <int kPerLane>
 __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *res,
                                                         __nv_bfloat16 *sum_out, __nv_bfloat16 *y,
                                                         const float *gamma, const float *beta,
                                                         int64_t rows, int D, float eps) {
-    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
+    const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
+    int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int chunks = D / 8;  // 16-byte chunks per row
-    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * D);
-    const uint4 *rr = res ? reinterpret_cast<const uint4 *>(res + row * D) : nullptr;
-    uint4 raw[kPerLane], rraw[kPerLane];
-#pragma unroll
-    for (int i = 0; i < kPerLane; ++i) {
-        const int c = lane + 32 * i;
-        if (c < chunks) {
-            raw[i] = xr[c];
-            if (rr) rraw[i] = rr[c];
-        }
-    }
-    float v[kPerLane][8];
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPerLane; ++i) {
-        const int c = lane + 32 * i;
-        if (c < chunks) {
-            const uint32_t wa[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                v[i][2 * u] = __uint_as_float(wa[u] << 16);
-                v[i][2 * u + 1] = __uint_as_float(wa[u] & 0xffff0000u);
-            }
-            if (rr) {
-                const uint32_t wb[4] = {rraw[i].x, rraw[i].y, rraw[i].z, rraw[i].w};
-                uint32_t pk[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const float s0 = v[i][2 * u] + __uint_as_float(wb[u] << 16);
-                    const float s1 = v[i][2 * u + 1] + __uint_as_float(wb[u] & 0xffff0000u);
-                    pk[u] = pack_bf16x2(s0, s1);
-                    v[i][2 * u] = __uint_as_float(pk[u] << 16);  // the rounded sum is what is normalised
-                    v[i][2 * u + 1] = __uint_as_float(pk[u] & 0xffff0000u);
-                }
-                if (sum_out) reinterpret_cast<uint4 *>(sum_out + row * D)[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) sum += v[i][e];
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float mean = sum / (float)D;
-    float sq = 0.f;
-#pragma unroll
-    for (int i = 0; i < kPerLane; ++i)
-        if (lane + 32 * i < chunks) {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float d = v[i][e] - mean;
-                sq = fmaf(d, d, sq);
-            }
-        }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float rstd = 1.f / sqrtf(sq / (float)D + eps);
-    uint4 *yr = reinterpret_cast<uint4 *>(y + row * D);
+    if (row >= rows) return;
+    float g[kPerLane][8], bb[kPerLane][8];  // this lane's gamma/beta, for all of the warp's rows
 #pragma unroll
     for (int i = 0; i < kPerLane; ++i) {
         const int c = lane + 32 * i;
@@ -518,14 +467,86 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const __nv_bfloat16 *x, 
             const float4 g1 = __ldg(reinterpret_cast<const float4 *>(gamma) + 2 * c + 1);
             const float4 b0 = __ldg(reinterpret_cast<const float4 *>(beta) + 2 * c);
             const float4 b1 = __ldg(reinterpret_cast<const float4 *>(beta) + 2 * c + 1);
-            const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-            uint32_t pk[4];
+            g[i][0] = g0.x; g[i][1] = g0.y; g[i][2] = g0.z; g[i][3] = g0.w;
+            g[i][4] = g1.x; g[i][5] = g1.y; g[i][6] = g1.z; g[i][7] = g1.w;
+            bb[i][0] = b0.x; bb[i][1] = b0.y; bb[i][2] = b0.z; bb[i][3] = b0.w;
+            bb[i][4] = b1.x; bb[i][5] = b1.y; bb[i][6] = b1.z; bb[i][7] = b1.w;
+        }
+    }
+    uint4 raw[kPerLane], rraw[kPerLane];
+    auto load_row = [&](int64_t r) {
+        const uint4 *xr = reinterpret_cast<const uint4 *>(x + r * D);
+        const uint4 *rr = res ? reinterpret_cast<const uint4 *>(res + r * D) : nullptr;
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-                pk[u] = pack_bf16x2((v[i][2 * u] - mean) * rstd * g[2 * u] + bb[2 * u],
-                                    (v[i][2 * u + 1] - mean) * rstd * g[2 * u + 1] + bb[2 * u + 1]);
-            yr[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int i = 0; i < kPerLane; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                raw[i] = xr[c];
+                if (rr) rraw[i] = rr[c];
+            }
+        }
+    };
+    load_row(row);
+    for (; row < rows; row += warps_total) {
+        float v[kPerLane][8];
+        float sum = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                const uint32_t wa[4] = {raw[i].x, raw[i].y, raw[i].z, raw[i].w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    v[i][2 * u] = __uint_as_float(wa[u] << 16);
+                    v[i][2 * u + 1] = __uint_as_float(wa[u] & 0xffff0000u);
+                }
+                if (res) {
+                    const uint32_t wb[4] = {rraw[i].x, rraw[i].y, rraw[i].z, rraw[i].w};
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float s0 = v[i][2 * u] + __uint_as_float(wb[u] << 16);
+                        const float s1 = v[i][2 * u + 1] + __uint_as_float(wb[u] & 0xffff0000u);
+                        pk[u] = pack_bf16x2(s0, s1);
+                        v[i][2 * u] = __uint_as_float(pk[u] << 16);  // the rounded sum is what is normalised
+                        v[i][2 * u + 1] = __uint_as_float(pk[u] & 0xffff0000u);
+                    }
+                    if (sum_out)
+                        reinterpret_cast<uint4 *>(sum_out + row * D)[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) sum += v[i][e];
+            }
+        }
+        if (row + warps_total < rows) load_row(row + warps_total);  // in flight during the reductions
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum / (float)D;
+        float sq = 0.f;
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i)
+            if (lane + 32 * i < chunks) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float d = v[i][e] - mean;
+                    sq = fmaf(d, d, sq);
+                }
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        const float rstd = 1.f / sqrtf(sq / (float)D + eps);
+        uint4 *yr = reinterpret_cast<uint4 *>(y + row * D);
+#pragma unroll
+        for (int i = 0; i < kPerLane; ++i) {
+            const int c = lane + 32 * i;
+            if (c < chunks) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    pk[u] = pack_bf16x2((v[i][2 * u] - mean) * rstd * g[i][2 * u] + bb[i][2 * u],
+                                        (v[i][2 * u + 1] - mean) * rstd * g[i][2 * u + 1] + bb[i][2 * u + 1]);
+                yr[c] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
         }
     }
 }

@@ -155,6 +155,13 @@ def test_tc_fp16(gae, ora):
     _check_tc(gae, ora, 1, 2, 384, 384, 128, True, dtype=torch.float16)
 
 
+@pytest.mark.parametrize("causal", [True, False])
+def test_tc_fp16_head_dim_64(gae, ora, causal):
+    """f16 at head_dim 64 (the tensor-core row sums read an f16 panel of
+    ones), ragged length."""
+    _check_tc(gae, ora, 2, 3, 333, 333, 64, causal, dtype=torch.float16)
+
+
 @pytest.mark.parametrize("q_offset,kv_offset", [(512, 0), (512, 256), (0, 512), (100, 37)])
 def test_tc_ring_block_offsets(gae, ora, q_offset, kv_offset):
     # A query block attending to one key block of a longer causal sequence.
@@ -237,7 +244,8 @@ def test_quantize_rows_int8_bit_exact(gae, ora):
 
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("causal", [False, True])
-def test_tc_scores_growing_along_keys(gae, ora, D, causal):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tc_scores_growing_along_keys(gae, ora, D, causal, dtype):
     """Keys whose scores grow along the sequence, so that a row's running max
     keeps rising by more than the lazy rescale's headroom from tile to tile:
     exercises the rebasing and the recomputation after a speculative tile."""
@@ -246,7 +254,7 @@ def test_tc_scores_growing_along_keys(gae, ora, D, causal):
     q = torch.randn(B, H, N, D, generator=g).abs()
     k = torch.randn(B, H, N, D, generator=g).abs() * torch.linspace(0.1, 3.0, N).view(1, 1, N, 1)
     v = torch.randn(B, H, N, D, generator=g)
-    q, k, v = (t.bfloat16() for t in (q, k, v))
+    q, k, v = (t.to(dtype) for t in (q, k, v))
     o, lse = gae.attention(q.cuda(), k.cuda(), v.cuda(), causal=causal, return_lse=True)
     torch.cuda.synchronize()
     gae.device_status()
