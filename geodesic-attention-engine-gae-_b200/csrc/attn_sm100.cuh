@@ -141,7 +141,11 @@ struct AttnCfg {
     static constexpr int kBarOffset = kOffOnes + kOnesBytes;
     // barriers: q_full, kv_full[S], kv_empty[S], s_full[2], p_full[2], o_full[2], done, q_empty,
     // q_full / q_empty of the second Q stage
-    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 2;
+    // P_i * V issued in two halves (head_dim 128: measured +0.4 to +1.6%;
+    // at 64 the f16 symphony layer lost 3%, so it stays whole there).
+    static constexpr bool kSplitPV = (D == 128);
+    // + p_half[2]: the first 64 keys of P_i written
+    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1 + 2 + 2;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;  // +align slack
     static constexpr uint32_t kTmemCols = 512;
     static constexpr uint32_t kColS0 = 0, kColS1 = 128, kColO0 = 256, kColO1 = 256 + kOCols;
@@ -206,6 +210,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
     auto bar_o = [&](int i) { return sBar + 8u * (5 + 2 * Cfg::kStages + i); };
     const uint32_t bar_done = sBar + 8u * (7 + 2 * Cfg::kStages);
     auto bar_q_empty = [&](int st) { return sBar + 8u * (st ? 10 + 2 * Cfg::kStages : 8 + 2 * Cfg::kStages); };
+    auto bar_p_half = [&](int i) { return sBar + 8u * (11 + 2 * Cfg::kStages + i); };
     uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(smem + Cfg::kBarOffset + Cfg::kNumBars * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
@@ -272,6 +277,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar_s(i), 1);
             mbar_init(bar_p(i), 128);
+            mbar_init(bar_p_half(i), 128);
             mbar_init(bar_o(i), 1);
         }
         mbar_init(bar_done, 1);
@@ -379,18 +385,42 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                                     smem_desc_sw128(kb + off, 16, 1024), idesc_qk, kk > 0);
                 }
             };
-            auto issue_pv = [&](int i, int slot, bool acc) {
+            // P_i * V in two halves of 64 keys: the first is issued as soon
+            // as the softmax group has written the first half of P_i (while
+            // it still computes the second), the second once all of P_i is
+            // there.  ph: phase parity of this tile's p_half / p_full.
+            auto issue_pv = [&](int i, int slot, bool acc, int ph) -> bool {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColO1 : Cfg::kColO0);
                 const uint32_t p_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
                 const uint32_t vb = sRing + slot * Cfg::kSlotBytes;
+                if constexpr (!Cfg::kSplitPV) {
+                    if (!mbar_wait(bar_p(i), ph, kSiteP, abort_flag)) return false;
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk) {
-                    umma_f16_ts(d_tmem, p_tmem + kk * 8,
-                                smem_desc_sw128(vb + kk * 16 * 128,
-                                                Cfg::kMmaRowSum ? (base + Cfg::kOffOnes) - vb : Cfg::kBoxBytes, 1024),
-                                idesc_pv,
-                                (acc || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk)
+                        umma_f16_ts(d_tmem, p_tmem + kk * 8,
+                                    smem_desc_sw128(vb + kk * 16 * 128,
+                                                    Cfg::kMmaRowSum ? (base + Cfg::kOffOnes) - vb : Cfg::kBoxBytes,
+                                                    1024),
+                                    idesc_pv, (acc || kk > 0) ? 1u : 0u);
+                    return true;
                 }
+                constexpr int kHalves = Cfg::kSplitPV ? 2 : 1;
+                for (int h = 0; h < kHalves; ++h) {
+                    if (!mbar_wait((h || !Cfg::kSplitPV) ? bar_p(i) : bar_p_half(i), ph, kSiteP, abort_flag))
+                        return false;
+                    tc_fence_after();
+#pragma unroll
+                    for (int k2 = 0; k2 < Cfg::kBlockN / 16 / kHalves; ++k2) {
+                        const int kk = h * (Cfg::kBlockN / 16 / kHalves) + k2;
+                        umma_f16_ts(d_tmem, p_tmem + kk * 8,
+                                    smem_desc_sw128(vb + kk * 16 * 128,
+                                                    Cfg::kMmaRowSum ? (base + Cfg::kOffOnes) - vb : Cfg::kBoxBytes,
+                                                    1024),
+                                    idesc_pv, (acc || kk > 0) ? 1u : 0u);
+                    }
+                }
+                return true;
             };
             bool ok = true;
             int ib = 0;  // ring item of this unit's K_0
@@ -413,11 +443,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     if (!ok) break;
                     if (j > 0) {
                         ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                             mbar_wait(bar_p(0), (gt0 + j - 1) & 1, kSiteP, abort_flag);
+                             issue_pv(0, v_slot, j - 1 > 0, (gt0 + j - 1) & 1);
                         if (!ok) break;
                         if (au == 0) GAE_TRACE(kTrMmaP0, j - 1);
-                        tc_fence_after();
-                        issue_pv(0, v_slot, j - 1 > 0);
                     }
                     if (!(x.skip0 && j == n_kv - 1) && !(early_qk0 && j == 0)) {
                         issue_qk(0, k_slot, q_base);
@@ -425,11 +453,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     }
                     if (au == 0) GAE_TRACE(kTrMmaIssued0, j);
                     if (j > 0) {
-                        ok = mbar_wait(bar_p(1), (gt1 + j - 1) & 1, kSiteP, abort_flag);
+                        ok = issue_pv(1, v_slot, j - 1 > 0, (gt1 + j - 1) & 1);
                         if (!ok) break;
                         if (au == 0) GAE_TRACE(kTrMmaP1, j - 1);
-                        tc_fence_after();
-                        issue_pv(1, v_slot, j - 1 > 0);
                         umma_commit(bar_kv_empty(v_slot));
                         // int8: both softmax groups have read K_{j-1}'s scales from its slot.
                         if (Cfg::kInt8) mbar_arrive(bar_kv_empty((k_item - 2) % Cfg::kStages));
@@ -447,9 +473,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 if (x.skip0) {
                     umma_commit(bar_o(0));  // PV0 of its last tile was issued in the loop
                 } else {
-                    if (!(ok = mbar_wait(bar_p(0), (gt0 + n_kv - 1) & 1, kSiteP, abort_flag))) break;
-                    tc_fence_after();
-                    issue_pv(0, v_slot, n_kv > 1);
+                    if (!(ok = issue_pv(0, v_slot, n_kv > 1, (gt0 + n_kv - 1) & 1))) break;
                     umma_commit(bar_o(0));
                 }
                 // Group 0 is done with this unit while group 1 still works on its
@@ -472,9 +496,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     }
                     break;
                 }
-                if (!(ok = mbar_wait(bar_p(1), (gt1 + n_kv - 1) & 1, kSiteP, abort_flag))) break;
-                tc_fence_after();
-                issue_pv(1, v_slot, n_kv > 1);
+                if (!(ok = issue_pv(1, v_slot, n_kv > 1, (gt1 + n_kv - 1) & 1))) break;
                 umma_commit(bar_o(1));
                 umma_commit(bar_kv_empty(v_slot));
                 if (Cfg::kInt8) mbar_arrive(bar_kv_empty((v_item - 1) % Cfg::kStages));
@@ -607,6 +629,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_tile);
                 m_run = m_tile;
             }
+            // Does O_i need rescaling this tile (warp-uniform)?  Then the
+            // first half of P_i is published only after the rescale below.
+            const bool rescale = Cfg::kSplitPV && j > 0 && __any_sync(0xffffffffu, alpha != 1.f);
             const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
             // p = 2^(s*sl2 - m): packed fp32x2 FMA, MUFU ex2, packed partial sums
             // (four independent pair accumulators).
@@ -631,6 +656,11 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     pk[e] = kBF16 ? pack_bf16x2(p0, p1) : pack_f16x2(p0, p1);
                 }
                 tmem_st16(tS + c * 16, pk);
+                if (Cfg::kSplitPV && c == 1 && !rescale) {  // the first 64 keys of P_i: their half of P_i * V may start
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(bar_p_half(grp));
+                }
             }
             if constexpr (!Cfg::kMmaRowSum) {
                 float a0, a1;
@@ -640,8 +670,9 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 (void)acc2;
             }
             // Rescale O_i when the base moved (warp-uniform: tcgen05.ld/st are
-            // warp-collective).  PV_i(j-1) has completed: its commit preceded S_i(j)'s.
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            // warp-collective), before any of this tile's P*V is issued.
+            // PV_i(j-1) has completed: its commit preceded S_i(j)'s.
+            if (Cfg::kSplitPV ? rescale : (j > 0 && __any_sync(0xffffffffu, alpha != 1.f))) {
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t r[32];
@@ -662,6 +693,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             }
             tmem_wait_st();
             tc_fence_before();
+            if (Cfg::kSplitPV && rescale) mbar_arrive(bar_p_half(grp));
             mbar_arrive(bar_p(grp));
             if (row == 0 && au == 0) GAE_TRACE(kTrPDone0 + grp, j);
         }
