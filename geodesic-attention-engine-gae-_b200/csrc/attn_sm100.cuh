@@ -389,12 +389,14 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
             // as the softmax group has written the first half of P_i (while
             // it still computes the second), the second once all of P_i is
             // there.  ph: phase parity of this tile's p_half / p_full.
-            auto issue_pv = [&](int i, int slot, bool acc, int ph) -> bool {
+            auto issue_pv = [&](int i, int slot, bool acc, int ph, int tr) -> bool {
                 const uint32_t d_tmem = tmem + (i ? Cfg::kColO1 : Cfg::kColO0);
                 const uint32_t p_tmem = tmem + (i ? Cfg::kColS1 : Cfg::kColS0);
                 const uint32_t vb = sRing + slot * Cfg::kSlotBytes;
+                (void)tr;
                 if constexpr (!Cfg::kSplitPV) {
                     if (!mbar_wait(bar_p(i), ph, kSiteP, abort_flag)) return false;
+                    if (tr >= 0) GAE_TRACE(kTrMmaP0 + i, tr);
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < Cfg::kBlockN / 16; ++kk)
@@ -409,6 +411,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 for (int h = 0; h < kHalves; ++h) {
                     if (!mbar_wait((h || !Cfg::kSplitPV) ? bar_p(i) : bar_p_half(i), ph, kSiteP, abort_flag))
                         return false;
+                    if (h == 0 && tr >= 0) GAE_TRACE(kTrMmaP0 + i, tr);
                     tc_fence_after();
 #pragma unroll
                     for (int k2 = 0; k2 < Cfg::kBlockN / 16 / kHalves; ++k2) {
@@ -443,9 +446,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     if (!ok) break;
                     if (j > 0) {
                         ok = mbar_wait(bar_kv_full(v_slot), (v_item / Cfg::kStages) & 1, kSiteKvFull, abort_flag) &&
-                             issue_pv(0, v_slot, j - 1 > 0, (gt0 + j - 1) & 1);
+                             issue_pv(0, v_slot, j - 1 > 0, (gt0 + j - 1) & 1, au == 0 ? j - 1 : -1);
                         if (!ok) break;
-                        if (au == 0) GAE_TRACE(kTrMmaP0, j - 1);
                     }
                     if (!(x.skip0 && j == n_kv - 1) && !(early_qk0 && j == 0)) {
                         issue_qk(0, k_slot, q_base);
@@ -453,9 +455,8 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     }
                     if (au == 0) GAE_TRACE(kTrMmaIssued0, j);
                     if (j > 0) {
-                        ok = issue_pv(1, v_slot, j - 1 > 0, (gt1 + j - 1) & 1);
+                        ok = issue_pv(1, v_slot, j - 1 > 0, (gt1 + j - 1) & 1, au == 0 ? j - 1 : -1);
                         if (!ok) break;
-                        if (au == 0) GAE_TRACE(kTrMmaP1, j - 1);
                         umma_commit(bar_kv_empty(v_slot));
                         // int8: both softmax groups have read K_{j-1}'s scales from its slot.
                         if (Cfg::kInt8) mbar_arrive(bar_kv_empty((k_item - 2) % Cfg::kStages));
@@ -473,7 +474,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                 if (x.skip0) {
                     umma_commit(bar_o(0));  // PV0 of its last tile was issued in the loop
                 } else {
-                    if (!(ok = issue_pv(0, v_slot, n_kv > 1, (gt0 + n_kv - 1) & 1))) break;
+                    if (!(ok = issue_pv(0, v_slot, n_kv > 1, (gt0 + n_kv - 1) & 1, -1))) break;
                     umma_commit(bar_o(0));
                 }
                 // Group 0 is done with this unit while group 1 still works on its
@@ -496,7 +497,7 @@ __global__ void __launch_bounds__(384, 1) attn_fwd_sm100_kernel(const __grid_con
                     }
                     break;
                 }
-                if (!(ok = issue_pv(1, v_slot, n_kv > 1, (gt1 + n_kv - 1) & 1))) break;
+                if (!(ok = issue_pv(1, v_slot, n_kv > 1, (gt1 + n_kv - 1) & 1, -1))) break;
                 umma_commit(bar_o(1));
                 umma_commit(bar_kv_empty(v_slot));
                 if (Cfg::kInt8) mbar_arrive(bar_kv_empty((v_item - 1) % Cfg::kStages));
