@@ -250,6 +250,9 @@ __global__ void __launch_bounds__(320, 1) linear_kernel(const __grid_constant__ 
 // TMEM holds its 128 rows of the two 256-column accumulators; each CTA's
 // eight epilogue warps drain its rows and arrive on the leader's
 // "accumulator empty" barrier.
+#ifndef GAE_LINEAR_RELAXED_ARRIVE
+#define GAE_LINEAR_RELAXED_ARRIVE 1
+#endif
 struct Linear2Cfg {
     static constexpr int BM = 256, BN = 256, BK = 64;  // pair tile
     static constexpr int kStages = 6;
@@ -422,8 +425,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(320, 1)
                     }
                 }
             }
+            // The accumulator is free once this thread's TMEM reads are done
+            // (each tcgen05.ld was waited for); its global stores need not be
+            // ordered before the MMA warp reuses the accumulator, so a relaxed
+            // arrive (a release would wait for the stores to complete).
             tc_fence_before();
+#if GAE_LINEAR_RELAXED_ARRIVE
+            mbar_arrive_remote_relaxed(mapa_shared(bar_acc_empty(b), 0));
+#else
             mbar_arrive_remote(mapa_shared(bar_acc_empty(b), 0));
+#endif
         }
     }
     tc_fence_before();
