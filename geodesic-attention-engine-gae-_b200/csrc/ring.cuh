@@ -293,8 +293,43 @@ gae_status ring_copy(const TS *src, const int64_t ss[3], TD *dst, const int64_t 
     return GAE_OK;
 }
 
+// Diagnostics: GAE_RING_PROFILE=1 prints each phase's device time (CUDA
+// events on the two streams) to stderr after every call.  Off by default.
+struct RingProfile {
+    bool on = false;
+    cudaEvent_t ev[64];
+    cudaStream_t evs[64];
+    const char *name[64];
+    int n = 0;
+    explicit RingProfile(bool enable) : on(enable) {}
+    void mark(const char *what, cudaStream_t stream) {
+        if (!on || n >= 64) return;
+        cudaEventCreate(&ev[n]);
+        cudaEventRecord(ev[n], stream);
+        evs[n] = stream;
+        name[n++] = what;
+    }
+    void report(int rank) {
+        if (!on) return;
+        for (int i = 0; i < n; ++i) cudaEventSynchronize(ev[i]);
+        for (int i = 1; i < n; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, ev[0], ev[i]);
+            fprintf(stderr, "[gae ring rank %d] %-24s at %9.3f ms\n", rank, name[i], ms);
+        }
+        for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
+        n = 0;
+    }
+};
+
 template <typename T>
 gae_status ring_run(gae_ring_ctx *c, const gae_attn_args *a, int zig, cudaStream_t st) {
+    static const bool prof_on = [] {
+        const char *e = getenv("GAE_RING_PROFILE");
+        return e && e[0] == '1';
+    }();
+    RingProfile prof(prof_on);
+    prof.mark("start", st);
     const int P = c->world, r = c->rank;
     const int64_t B = a->batch, H = a->heads, S = a->seq_q, D = a->head_dim, BH = B * H;
     const int64_t C = zig ? S / 2 : S;
@@ -391,6 +426,7 @@ gae_status ring_run(gae_ring_ctx *c, const gae_attn_args *a, int zig, cudaStream
         }
     }
 
+    prof.mark("re-deal in done", st);
     // ---- accumulator: O = 0, LSE = -inf
     GAE_CUDA_TRY(cudaMemsetAsync(acc, 0, act * 4, st));
     gae::ring_fill_kernel<<<256, 256, 0, st>>>(lacc, BH * S, -INFINITY);
@@ -413,6 +449,7 @@ gae_status ring_run(gae_ring_ctx *c, const gae_attn_args *a, int zig, cudaStream
                 return s;
             if ((s = nccl_settle(c, c->nc->GroupEnd(), "K/V exchange")) != GAE_OK) return s;
             GAE_CUDA_TRY(cudaEventRecord(c->ev_b, c->comm_st));
+            prof.mark("  K/V exchange done", c->comm_st);
         }
         RingOp ops[2];
         const int n_ops = ring_plan(r, P, t, a->causal, zig, S, ops);
@@ -441,6 +478,7 @@ gae_status ring_run(gae_ring_ctx *c, const gae_attn_args *a, int zig, cudaStream
                                                                                  S, op.q_row0, total, (int)D);
             GAE_CUDA_TRY(cudaGetLastError());
         }
+        prof.mark("step compute done", st);
         if (t < P - 1) GAE_CUDA_TRY(cudaStreamWaitEvent(st, c->ev_b, 0));  // the next block has arrived
     }
 
@@ -507,6 +545,8 @@ gae_status ring_run(gae_ring_ctx *c, const gae_attn_args *a, int zig, cudaStream
                 return s;
         }
     }
+    prof.mark("re-deal out done", st);
+    prof.report(c->rank);
     return GAE_OK;
 }
 
