@@ -357,8 +357,8 @@ def run_reference_kernel(args, w):
         L = oracle.ref_symphony128()
         fwd = getattr(L, f"ref_symphony{D}_fwd", None) if L is not None else None
     if fwd is None:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "reference symphony kernel not built (oracle/_ref missing)"}))
+        emit({"impl": "reference", "unavailable":
+                          "reference symphony kernel not built (oracle/_ref missing)"})
         return 0
     a = {n_: torch.from_numpy(v_).cuda() for n_, v_ in symphony_arrays(N, D, 1000).items()}
     out = torch.empty_like(a["x"])
@@ -383,10 +383,10 @@ def run_reference_kernel(args, w):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     value = symphony_flops(N, D) / (ms * 1e-3) / 1e12
-    print(json.dumps({"impl": "reference", "kind": "reference-gpu-kernel",
+    emit({"impl": "reference", "kind": "reference-gpu-kernel",
                       "metric": w.get("metric", METRIC), "value": value, "unit": "TFLOPS",
                       "ms_per_step": ms, "steps": steps, "n_gpus": 1,
-                      "config": {"workload": w["cfg"], "seq_len": N, "head_dim": D}}), flush=True)
+                      "config": {"workload": w["cfg"], "seq_len": N, "head_dim": D}})
     return 0
 
 
@@ -401,8 +401,8 @@ def run_reference_chain(args, w):
     from oracle import oracle
     L = oracle.ref_kernel_bench()
     if L is None:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "reference kernel chain not built (oracle/_ref missing)"}))
+        emit({"impl": "reference", "unavailable":
+                          "reference kernel chain not built (oracle/_ref missing)"})
         return 0
     if int(os.environ.get("RANK", "0")) != 0:
         return 0
@@ -416,7 +416,7 @@ def run_reference_chain(args, w):
     ref_tflops = float(L.ref_kernel_bench_tflops(N, D, best, iters))
     ms_head = 4.0 * N * N * D / (ref_tflops * 1e12) * 1e3
     ours = attn_flops(1, 1, N, N, D, w["causal"]) / (ms_head * 1e-3) / 1e12
-    print(json.dumps({"impl": "reference", "kind": "reference-gpu-kernel-chain",
+    emit({"impl": "reference", "kind": "reference-gpu-kernel-chain",
                       "metric": w.get("metric", METRIC), "value": ours, "unit": "TFLOPS",
                       "value_reference_convention": ref_tflops,
                       "flop_conventions": {"value": "4*d per visible (causal) pair",
@@ -424,8 +424,7 @@ def run_reference_chain(args, w):
                       "ms_per_head": ms_head, "tile": best,
                       "tile_sweep_reference_convention": sweep, "steps": iters, "n_gpus": 1,
                       "dtype": "f16", "config": {"workload": w["cfg"], "seq_len": N, "head_dim": D,
-                                                 "heads_timed_as": "one sequence, scaled by B*H"}}),
-          flush=True)
+                                                 "heads_timed_as": "one sequence, scaled by B*H"}})
     return 0
 
 
@@ -442,11 +441,29 @@ def _print_reference(args, w, value, sec, desc, threads):
         "e2e": {"value": value, "unit": "TFLOPS", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
     return 0
 
 
+_JSON_FD = None
+
+
+def emit(line: dict):
+    """Prints the one JSON result line on the process's real stdout."""
+    text = json.dumps(line) + "\n"
+    if _JSON_FD is None:
+        print(text, end="", flush=True)
+    else:
+        os.write(_JSON_FD, text.encode())
+
+
 def main():
+    # Everything else that reaches file descriptor 1 (libraries' banners,
+    # e.g. NCCL's version line) goes to stderr; the JSON line keeps stdout.
+    global _JSON_FD
+    sys.stdout.flush()
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
@@ -811,7 +828,7 @@ def main():
         t_s = ms_step * 1e-3
         line["pct_of_peak_split"] = 100.0 * (flops / 2 / (2 * peak * 1e12) + flops / 2 / (peak * 1e12)) / t_s
         line["pct_of_peak_split_note"] = "QK^T ops / (2 x measured bf16 peak) + PV FLOP / bf16 peak, over the step time"
-    print(json.dumps(line), flush=True)
+    emit(line)
     if world > 1:
         dist.destroy_process_group()
     return 0

@@ -1244,9 +1244,21 @@ gae_status gae_ring_unique_id(void *unique_id) {
 }
 
 gae_status gae_ring_ctx_create(const void *unique_id, int rank, int world, double timeout_s, gae_ring_ctx **out) {
-    if (!out || !unique_id) return fail(GAE_ERR_INVALID_ARG, "NULL argument");
+    if (!out || (!unique_id && world > 1)) return fail(GAE_ERR_INVALID_ARG, "NULL argument");
     *out = nullptr;
     if (world < 1 || rank < 0 || rank >= world) return fail(GAE_ERR_INVALID_ARG, "rank %d of world %d", rank, world);
+    if (world == 1) {  // the whole sequence is local: no communicator (and no NCCL) needed
+        gae_ring_ctx *c = new gae_ring_ctx();
+        c->world = 1;
+        c->timeout_s = timeout_s;
+        gae_status s = ring_ctx_init_common(c);
+        if (s != GAE_OK) {
+            ring_ctx_release(c);
+            return s;
+        }
+        *out = c;
+        return GAE_OK;
+    }
     const NcclApi *nc = nccl_api();
     if (!nc) return fail(GAE_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
     gae_ring_ctx *c = new gae_ring_ctx();

@@ -147,7 +147,7 @@ def ring_context(group=None, timeout_s: float = RING_TIMEOUT_S):
     P = dist.get_world_size(group) if dist.is_initialized() else 1
     r = dist.get_rank(group) if dist.is_initialized() else 0
     uid = (C.c_ubyte * 128)()
-    if r == 0:
+    if r == 0 and P > 1:  # one rank needs no communicator
         _check(lib().gae_ring_unique_id(uid))
     if P > 1:
         obj = [bytes(uid)]

@@ -234,7 +234,8 @@ typedef struct gae_ring_ctx gae_ring_ctx;
 GAE_API gae_status gae_ring_unique_id(void *unique_id);
 
 /* Joins the P-rank communicator of unique_id as `rank` (collective: every
- * rank calls it). */
+ * rank calls it).  With world == 1 no communicator is made (unique_id is
+ * not read, NCCL is not loaded). */
 GAE_API gae_status gae_ring_ctx_create(const void *unique_id, int rank, int world, double timeout_s,
                                        gae_ring_ctx **ctx);
 
