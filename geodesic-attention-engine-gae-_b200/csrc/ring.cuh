@@ -36,11 +36,11 @@ namespace gae {
 // dst[b, h, s, :] = src[b, h, s, :] for s < rows over [B, H, rows, D] views
 // with element strides {b, h, s} on both sides (head_dim contiguous); the
 // element types may differ (fp32 accumulator -> 16-bit output).  One warp a
-// row.
+// row; vec4: D, every stride and both bases allow 4-element vector accesses.
 template <typename TS, typename TD>
 __global__ void ring_copy_rows_kernel(const TS *__restrict__ src, int64_t ssb, int64_t ssh, int64_t sss,
                                       TD *__restrict__ dst, int64_t dsb, int64_t dsh, int64_t dss,
-                                      int H, int64_t rows, int64_t total_rows, int D) {
+                                      int H, int64_t rows, int64_t total_rows, int D, int vec4) {
     const int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (g >= total_rows) return;
     const int lane = threadIdx.x & 31;
@@ -48,6 +48,30 @@ __global__ void ring_copy_rows_kernel(const TS *__restrict__ src, int64_t ssb, i
     const int64_t b = bh / H, h = bh % H;
     const TS *sr = src + b * ssb + h * ssh + s * sss;
     TD *dr = dst + b * dsb + h * dsh + s * dss;
+    if (vec4) {  // four elements a lane, one vector load and store each
+        for (int c = 4 * lane; c < D; c += 128) {
+            float f[4];
+            if constexpr (sizeof(TS) == 4) {
+                const float4 x = *reinterpret_cast<const float4 *>(sr + c);
+                f[0] = x.x; f[1] = x.y; f[2] = x.z; f[3] = x.w;
+            } else {
+                const uint2 x = *reinterpret_cast<const uint2 *>(sr + c);
+                const TS *e = reinterpret_cast<const TS *>(&x);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) f[u] = to_f<TS>(e[u]);
+            }
+            if constexpr (sizeof(TD) == 4) {
+                *reinterpret_cast<float4 *>(dr + c) = make_float4(f[0], f[1], f[2], f[3]);
+            } else {
+                uint2 y;
+                TD *e = reinterpret_cast<TD *>(&y);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) e[u] = from_f<TD>(f[u]);
+                *reinterpret_cast<uint2 *>(dr + c) = y;
+            }
+        }
+        return;
+    }
     for (int c = lane; c < D; c += 32) dr[c] = from_f<TD>(to_f<TS>(sr[c]));
 }
 
@@ -287,8 +311,11 @@ gae_status ring_copy(const TS *src, const int64_t ss[3], TD *dst, const int64_t 
     const int64_t total = B * H * rows;
     if (total == 0) return GAE_OK;
     const int warps = 8;
+    auto al = [](const void *p, size_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+    const int vec4 = (D % 4 == 0) && al(src, 4 * sizeof(TS)) && al(dst, 4 * sizeof(TD)) && ss[0] % 4 == 0 &&
+                     ss[1] % 4 == 0 && ss[2] % 4 == 0 && ds[0] % 4 == 0 && ds[1] % 4 == 0 && ds[2] % 4 == 0;
     gae::ring_copy_rows_kernel<TS, TD><<<(unsigned)((total + warps - 1) / warps), warps * 32, 0, st>>>(
-        src, ss[0], ss[1], ss[2], dst, ds[0], ds[1], ds[2], (int)H, rows, total, (int)D);
+        src, ss[0], ss[1], ss[2], dst, ds[0], ds[1], ds[2], (int)H, rows, total, (int)D, vec4);
     GAE_CUDA_TRY(cudaGetLastError());
     return GAE_OK;
 }
