@@ -188,11 +188,12 @@ gae_status launch_attn_tc(const gae_attn_args *a, cudaStream_t st) {
     // gain most from keeping TMEM, barriers and the K/V stream alive, measured
     // +20%).  head_dim 128: one CTA per unit, balanced by the hardware's block
     // scheduler (equal or better under the power cap, measured).
-    // Non-causal head_dim 128 (config 2 non-causal, the ring's off-diagonal
-    // blocks): a persistent head-major grid, measured +1.5% (1284 vs 1267);
-    // causal head_dim 128 stays one CTA per unit (1157 vs 1107 persistent).
-    bool persistent = (D == 64 || !a->causal) && units > num_sms();
-    p.head_major = (persistent && D == 64) ? 0 : 1;
+    // head_dim 128 stays one CTA per unit, causal and not: a persistent
+    // head-major grid gave config 2 non-causal +1.5% (1284 vs 1267) alone,
+    // but the two-GPU ring, whose off-diagonal steps are non-causal, ran at
+    // 2220 against 2256 with it (power-capped, NCCL's kernels beside it).
+    bool persistent = D == 64 && units > num_sms();
+    p.head_major = persistent ? 0 : 1;
     {
         // Diagnostics overrides of the schedule: GAE_ATTN_PERSISTENT=0/1 and
         // GAE_ATTN_HEAD_MAJOR=0/1 (unit order of the persistent grid).
